@@ -1,0 +1,22 @@
+"""B200 (sm_100a) DeepSeek-V3/R1 FP8 block-scaled MoE forward.
+
+The package directory name starts with a digit, so import it with
+``importlib.import_module("15642_moe_b200")``.
+
+Public surface (mirrors the reference's Python API):
+  run(**inputs)                  drop-in for reference.run (reference/moe_ref.py:5)
+  run_custom(ops, **inputs)      moe_layer.py:99
+  pack_w13 / pack_w2 / moe_forward  the extension functions of kernels/moe.cu:902-909
+  route(logits, bias, rsf)       the device router alone (expert indices + weights)
+  make_inputs(cfg, device)       seeded synthetic inputs of the benchmark configurations
+"""
+from .layer import (_cached_pack, _load_custom_ops, moe_forward, ops, pack_w13, pack_w2, route,
+                    run, run_custom, workspace_bytes)
+from .synth import CONFIGS, MoEConfig, make_inputs, quantile_table
+from ._native import MoEError, device_status, workspace_layout
+
+__all__ = [
+    "run", "run_custom", "ops", "pack_w13", "pack_w2", "moe_forward", "route", "workspace_bytes",
+    "make_inputs", "MoEConfig", "CONFIGS", "quantile_table", "MoEError", "device_status",
+    "workspace_layout", "_cached_pack", "_load_custom_ops",
+]

@@ -1,0 +1,224 @@
+/*
+ * GEMM2 with the routing weight over the routed rows of every active local expert
+ * (reference/moe_ref.py:131-134: O = C . W2[e]^T, contribution = O * w[token, e]).
+ *
+ * C arrives from GEMM1 as two e4m3 terms sharing one fp32 scale per (row, 128-block):
+ * C ~= scale * (hi + lo). Both terms are multiplied against the same W2 tile and accumulate
+ * into the same TMEM accumulator (8 x tcgen05.mma per 128-K block), so the intermediate
+ * keeps ~2^-8 relative precision instead of e4m3's 2^-4 while W2 stays FP8 in HBM.
+ *
+ * Work unit = (128-row tile, 256-column tile of H). Same warp roles as GEMM1:
+ *   warp 0 producer (bulk copies: 16 KB hi + 16 KB lo + 32 KB W2 per stage, 3 stages),
+ *   warp 1 MMA issuer, warps 4-11 epilogue (per-128-K promotion with c_scale * w2_scale,
+ *   final multiply by the route weight, fp32 rows written to the partial buffer).
+ */
+#pragma once
+#include "moe_common.cuh"
+
+namespace moe {
+
+struct Gemm2Args {
+  const uint8_t* c_hi;      // [tiles, 16, 128, 128] SW128
+  const uint8_t* c_lo;      // [tiles, 16, 128, 128] SW128
+  const float* c_scale;     // [tiles, 16, 128]
+  const uint8_t* w2p;       // [E, 28, 16, 256, 128] SW128 (packed by pack_w2_kernel)
+  const float* w2_scale;    // [E, 56, 16]
+  const int* tile_expert;   // [tiles]
+  const int* tile_rows;     // [tiles]
+  const int* n_tiles;       // [1]
+  int tiles_max;            // capacity of the workspace tile arrays
+  int E_local;              // number of local experts (bounds of tile_expert)
+  const float* route_w;     // [tiles * 128]
+  float* partial;           // [tiles * 128, 7168]
+};
+
+constexpr int G2_STAGES = 3;
+constexpr int G2_A_BYTES = TILE_BYTES;      // one of hi / lo
+constexpr int G2_B_BYTES = 2 * TILE_BYTES;  // 256 W2 rows x 128 K bytes
+constexpr int G2_STAGE_BYTES = 2 * G2_A_BYTES + G2_B_BYTES;
+constexpr int G2_THREADS = GEMM_THREADS;
+constexpr int G2_CTRL_BYTES = 1024;
+constexpr int G2_SMEM = G2_STAGES * G2_STAGE_BYTES + G2_CTRL_BYTES + 1024;
+
+struct G2Ctrl {
+  uint64_t full[G2_STAGES];
+  uint64_t empty[G2_STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+static_assert(sizeof(G2Ctrl) <= G2_CTRL_BYTES, "control block too large");
+
+__global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(Gemm2Args p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = align_1024(smem_raw);
+  G2Ctrl* ctl = reinterpret_cast<G2Ctrl*>(smem + G2_STAGES * G2_STAGE_BYTES);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int n_units = clamp_tiles(*p.n_tiles, p.tiles_max) * G2_NT;
+  if (static_cast<int>(blockIdx.x) >= n_units) return;
+
+  if (threadIdx.x == 0) {
+#pragma unroll
+    for (int s = 0; s < G2_STAGES; ++s) {
+      mbar_init(&ctl->full[s], 1);
+      mbar_init(&ctl->empty[s], 1);
+    }
+#pragma unroll
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&ctl->tfull[b], 1);
+      mbar_init(&ctl->tempty[b], 8);
+    }
+    mbar_init(&ctl->mma_done, 1);
+    ctl->abort_flag = 0;
+    fence_mbar_init();
+  }
+  if (warp == 1) {
+    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = ctl->tmem_base;
+  volatile int* abort_flag = &ctl->abort_flag;
+
+  if (warp < 4) {
+    regs_dec<REGS_CTRL>();
+  }
+  if (warp == 0) {
+    // ---------------- producer ----------------
+    if (lane == 0) {
+      const uint64_t pol_w = policy_evict_first();
+      uint32_t it = 0;
+      for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
+        const int tile = u / G2_NT, nt = u % G2_NT;
+        const int e = checked_expert(p.tile_expert[tile], p.E_local);
+        const size_t a_off = static_cast<size_t>(tile) * IB * TILE_BYTES;
+        const uint8_t* b_src = p.w2p + (static_cast<size_t>(e) * G2_NT + nt) * IB * G2_B_BYTES;
+        for (int ib = 0; ib < IB; ++ib, ++it) {
+          const int s = it % G2_STAGES;
+          const uint32_t ph = (it / G2_STAGES) & 1u;
+          if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) break;
+          uint8_t* st = smem + s * G2_STAGE_BYTES;
+          mbar_arrive_expect_tx(&ctl->full[s], G2_STAGE_BYTES);
+          bulk_g2s(st, p.c_hi + a_off + static_cast<size_t>(ib) * TILE_BYTES, G2_A_BYTES,
+                   &ctl->full[s]);
+          bulk_g2s(st + G2_A_BYTES, p.c_lo + a_off + static_cast<size_t>(ib) * TILE_BYTES,
+                   G2_A_BYTES, &ctl->full[s]);
+          bulk_g2s_hint(st + 2 * G2_A_BYTES, b_src + static_cast<size_t>(ib) * G2_B_BYTES,
+                        G2_B_BYTES, &ctl->full[s], pol_w);
+        }
+      }
+      const uint32_t issued = it;
+      if (!*abort_flag) {
+        for (uint32_t jt = issued; jt < issued + G2_STAGES; ++jt) {
+          if (!mbar_wait(&ctl->empty[jt % G2_STAGES], ((jt / G2_STAGES) & 1u) ^ 1u, abort_flag,
+                         ST_TIMEOUT_PRODUCER))
+            break;
+        }
+      }
+      if (*abort_flag) {
+        for (uint32_t i = 1; i <= G2_STAGES && i <= issued; ++i) {
+          const uint32_t jt = issued - i;
+          mbar_wait_drain(&ctl->full[jt % G2_STAGES], (jt / G2_STAGES) & 1u);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------- MMA issuer ----------------
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
+      uint32_t it = 0;
+      for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
+        for (int ib = 0; ib < IB; ++ib, ++it) {
+          const int s = it % G2_STAGES;
+          const uint32_t ph = (it / G2_STAGES) & 1u;
+          const uint32_t b = it & 1u, use = it >> 1;
+          if (!mbar_wait(&ctl->tempty[b], (use & 1u) ^ 1u, abort_flag, ST_TIMEOUT_MMA)) break;
+          if (!mbar_wait(&ctl->full[s], ph, abort_flag, ST_TIMEOUT_MMA)) break;
+          tc_fence_after();
+          const uint32_t hi_addr = smem_u32(smem + s * G2_STAGE_BYTES);
+          const uint32_t lo_addr = hi_addr + G2_A_BYTES;
+          const uint32_t b_addr = hi_addr + 2 * G2_A_BYTES;
+          const uint32_t d = tmem + b * 256u;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t bd = sdesc_k_sw128(b_addr + kk * 32);
+            tc_mma_f8(d, sdesc_k_sw128(hi_addr + kk * 32), bd, idesc, kk > 0 ? 1u : 0u);
+            tc_mma_f8(d, sdesc_k_sw128(lo_addr + kk * 32), bd, idesc, 1u);
+          }
+          tc_commit(&ctl->empty[s]);
+          tc_commit(&ctl->tfull[b]);
+        }
+      }
+      if (*abort_flag) {
+        tc_commit(&ctl->mma_done);
+        mbar_wait_drain(&ctl->mma_done, 0);
+      }
+    }
+  } else if (warp >= 4) {
+    // ---------------- epilogue (warps 4..11) ----------------
+    regs_inc<REGS_EPI>();
+    const int q = warp & 3;
+    const int hf = (warp - 4) >> 2;    // which 128 of the 256 output columns
+    const int row = q * 32 + lane;
+    const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+    uint32_t it = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+      const int tile = u / G2_NT, nt = u % G2_NT;
+      const int e = checked_expert(p.tile_expert[tile], p.E_local);
+      const int hb = nt * 2 + hf;
+      const float* cs_ptr = p.c_scale + static_cast<size_t>(tile) * IB * TILE_M + row;
+      const float* ws_ptr = p.w2_scale + (static_cast<size_t>(e) * HB + hb) * IB;
+      float acc[128];
+#pragma unroll
+      for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
+      float cs_next = __ldg(cs_ptr);
+      bool aborted = false;
+      for (int ib = 0; ib < IB; ++ib, ++it) {
+        const float cs = cs_next;
+        if (ib + 1 < IB) cs_next = __ldg(cs_ptr + (ib + 1) * TILE_M);
+        const float f = cs * __ldg(ws_ptr + ib);
+        const uint32_t b = it & 1u, use = it >> 1;
+        if (!mbar_wait_warp(&ctl->tfull[b], use & 1u, abort_flag, ST_TIMEOUT_EPILOGUE)) {
+          aborted = true;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t base = tmem + t_lane + b * 256u + hf * 128u;
+        float v[32];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          tmem_ld32(base + c * 32u, v);
+#pragma unroll
+          for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(v[i], f, acc[c * 32 + i]);
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->tempty[b]);
+      }
+      if (named_bar_or(1, 256, aborted)) break;
+
+      if (row < p.tile_rows[tile]) {
+        const float w = p.route_w[static_cast<size_t>(tile) * TILE_M + row];
+        float4* dst = reinterpret_cast<float4*>(p.partial +
+                                                (static_cast<size_t>(tile) * TILE_M + row) * H +
+                                                nt * 256 + hf * 128);
+#pragma unroll
+        for (int i = 0; i < 32; ++i)
+          dst[i] = make_float4(acc[4 * i] * w, acc[4 * i + 1] * w, acc[4 * i + 2] * w,
+                               acc[4 * i + 3] * w);
+      }
+    }
+  }
+
+  __syncwarp();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 1) tmem_dealloc(tmem, 512);
+}
+
+}  // namespace moe

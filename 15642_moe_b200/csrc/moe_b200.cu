@@ -1,0 +1,276 @@
+/*
+ * The one translation unit of libmoe_b200.so: every kernel plus the extern "C" boundary
+ * declared in include/moe_b200.h.
+ *
+ * moe_forward pipeline (one stream, no host synchronisation):
+ *   memset(counts) -> route_kernel -> dispatch_kernel -> gather_kernel
+ *   -> gemm1_swiglu_kernel (tcgen05) -> gemm2_weighted_kernel (tcgen05) -> combine_kernel
+ * replacing the reference's route_dispatch / stage1 / stage2 / bf16_convert launches
+ * (kernels/moe.cu:842-897).
+ */
+#include "moe_common.cuh"
+
+#include "route.cuh"
+#include "gemm1.cuh"
+#include "gemm2.cuh"
+#include "pack.cuh"
+#include "synth.cuh"
+#include "moe_b200.h"
+
+#include <mutex>
+#include <string>
+
+using namespace moe;
+
+namespace {
+
+thread_local std::string g_err;
+
+int fail(int code, const std::string& msg) {
+  g_err = msg;
+  return code;
+}
+
+int cuda_check(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return MOE_OK;
+  return fail(MOE_ERR_CUDA, std::string(what) + ": " + cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+struct DeviceInfo {
+  bool ready = false;
+  int num_sms = 0;
+};
+std::mutex g_dev_mu;
+DeviceInfo g_dev[64];
+
+// Per-device one-time set-up: SM count and the large dynamic shared-memory opt-in.
+int device_info(DeviceInfo** out) {
+  int dev = 0;
+  if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  if (dev < 0 || dev >= 64) return fail(MOE_ERR_CUDA, "device ordinal out of range");
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  DeviceInfo& d = g_dev[dev];
+  if (!d.ready) {
+    if (int rc = cuda_check(cudaDeviceGetAttribute(&d.num_sms, cudaDevAttrMultiProcessorCount, dev),
+                            "cudaDeviceGetAttribute"))
+      return rc;
+    if (int rc = cuda_check(cudaFuncSetAttribute(gemm1_swiglu_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, G1_SMEM),
+                            "cudaFuncSetAttribute(gemm1)"))
+      return rc;
+    if (int rc = cuda_check(cudaFuncSetAttribute(gemm2_weighted_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, G2_SMEM),
+                            "cudaFuncSetAttribute(gemm2)"))
+      return rc;
+    // setmaxnreg.inc in the epilogue warpgroups only completes if the CTA was launched with
+    // enough registers for the whole split; refuse to launch a build where it could stall.
+    cudaFuncAttributes fa1{}, fa2{};
+    if (int rc = cuda_check(cudaFuncGetAttributes(&fa1, gemm1_swiglu_kernel), "cudaFuncGetAttributes(gemm1)")) return rc;
+    if (int rc = cuda_check(cudaFuncGetAttributes(&fa2, gemm2_weighted_kernel), "cudaFuncGetAttributes(gemm2)")) return rc;
+    if (fa1.numRegs < GEMM_LAUNCH_REGS_MIN || fa2.numRegs < GEMM_LAUNCH_REGS_MIN)
+      return fail(MOE_ERR_CUDA, "GEMM kernels built with " + std::to_string(fa1.numRegs) + "/" +
+                                    std::to_string(fa2.numRegs) + " registers per thread; the warpgroup "
+                                    "register split needs " + std::to_string(GEMM_LAUNCH_REGS_MIN));
+    d.ready = true;
+  }
+  *out = &d;
+  return MOE_OK;
+}
+
+int grid_for(size_t work, int per_block, int cap) {
+  size_t g = (work + per_block - 1) / per_block;
+  if (g < 1) g = 1;
+  if (g > static_cast<size_t>(cap)) g = cap;
+  return static_cast<int>(g);
+}
+
+}  // namespace
+
+extern "C" {
+
+const char* moe_last_error(void) { return g_err.c_str(); }
+
+int moe_get_status(int* status, int reset) {
+  if (status == nullptr) return fail(MOE_ERR_INVALID, "status must not be null");
+  if (int rc = cuda_check(cudaDeviceSynchronize(), "cudaDeviceSynchronize")) return rc;
+  int v = 0;
+  if (int rc = cuda_check(cudaMemcpyFromSymbol(&v, g_status, sizeof(int)), "read status")) return rc;
+  *status = v;
+  if (reset) {
+    const int zero = 0;
+    if (int rc = cuda_check(cudaMemcpyToSymbol(g_status, &zero, sizeof(int)), "reset status")) return rc;
+  }
+  return MOE_OK;
+}
+
+size_t moe_pack_w13_bytes(int E_local) {
+  return E_local > 0 ? static_cast<size_t>(E_local) * G1N * H : 0;
+}
+
+size_t moe_pack_w2_bytes(int E_local) {
+  return E_local > 0 ? static_cast<size_t>(E_local) * H * I : 0;
+}
+
+int moe_pack_w13(const void* w13, int E_local, void* w13_packed, void* stream) {
+  if (E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "W13 must be [E_local, 4096, 7168]");
+  if (w13 == nullptr || w13_packed == nullptr) return fail(MOE_ERR_INVALID, "W13 must not be null");
+  if (!aligned16(w13) || !aligned16(w13_packed)) return fail(MOE_ERR_INVALID, "W13 must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const size_t chunks = static_cast<size_t>(E_local) * G1_NT * 256 * (H / 16);
+  pack_w13_kernel<<<grid_for(chunks, 256, d->num_sms * 16), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(w13), E_local, static_cast<uint8_t*>(w13_packed));
+  return cuda_check(cudaGetLastError(), "pack_w13_kernel launch");
+}
+
+int moe_pack_w2(const void* w2, int E_local, void* w2_packed, void* stream) {
+  if (E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "W2 must be [E_local, 7168, 2048]");
+  if (w2 == nullptr || w2_packed == nullptr) return fail(MOE_ERR_INVALID, "W2 must not be null");
+  if (!aligned16(w2) || !aligned16(w2_packed)) return fail(MOE_ERR_INVALID, "W2 must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const size_t chunks = static_cast<size_t>(E_local) * G2_NT * 256 * (I / 16);
+  pack_w2_kernel<<<grid_for(chunks, 256, d->num_sms * 16), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint8_t*>(w2), E_local, static_cast<uint8_t*>(w2_packed));
+  return cuda_check(cudaGetLastError(), "pack_w2_kernel launch");
+}
+
+size_t moe_forward_workspace_bytes(int T, int E_local) {
+  if (T < 0 || E_local < 1 || E_local > E_GLOBAL) return 0;
+  return make_workspace(T, E_local).total;
+}
+
+int moe_workspace_layout(int T, int E_local, size_t* offsets, int n) {
+  if (T < 0 || E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "bad T or E_local");
+  const Workspace w = make_workspace(T, E_local);
+  const size_t v[17] = {w.counts,      w.n_tiles,   w.topk_idx,    w.topk_w,  w.token_nr, w.token_row,
+                        w.tile_expert, w.tile_rows, w.route_token, w.route_w, w.a_tiled,  w.a_scale,
+                        w.c_hi,        w.c_lo,      w.c_scale,     w.partial, w.total};
+  for (int i = 0; i < n && i < 17; ++i) offsets[i] = v[i];
+  return 17;
+}
+
+int moe_forward(const void* hidden, const float* hidden_scale, const void* w13_packed,
+                const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                const float* logits, const float* bias, float routed_scaling_factor,
+                int local_expert_offset, int T, int E_local, void* out_bf16, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  if (T < 0) return fail(MOE_ERR_INVALID, "hidden must be [T, 7168]");
+  if (E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "W13_packed must be [E_local, ...] with 1 <= E_local <= 256");
+  if (T == 0) return MOE_OK;
+  if (!hidden || !hidden_scale || !w13_packed || !w13_scale || !w2_packed || !w2_scale || !logits ||
+      !bias || !out_bf16 || !workspace)
+    return fail(MOE_ERR_INVALID, "moe_forward: null pointer argument");
+  const void* ptrs[] = {hidden, hidden_scale, w13_packed, w13_scale, w2_packed, w2_scale, logits, bias, out_bf16, workspace};
+  for (const void* q : ptrs)
+    if (!aligned16(q)) return fail(MOE_ERR_INVALID, "moe_forward: every tensor must be 16-byte aligned");
+  const Workspace ws = make_workspace(T, E_local);
+  if (workspace_bytes < ws.total)
+    return fail(MOE_ERR_WORKSPACE, "workspace too small: need " + std::to_string(ws.total) + " bytes");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* W = static_cast<uint8_t*>(workspace);
+  int* counts = reinterpret_cast<int*>(W + ws.counts);
+  int* n_tiles = reinterpret_cast<int*>(W + ws.n_tiles);
+  int* topk_idx = reinterpret_cast<int*>(W + ws.topk_idx);
+  float* topk_w = reinterpret_cast<float*>(W + ws.topk_w);
+  int* token_nr = reinterpret_cast<int*>(W + ws.token_nr);
+  int* token_row = reinterpret_cast<int*>(W + ws.token_row);
+  int* tile_expert = reinterpret_cast<int*>(W + ws.tile_expert);
+  int* tile_rows = reinterpret_cast<int*>(W + ws.tile_rows);
+  int* route_token = reinterpret_cast<int*>(W + ws.route_token);
+  float* route_w = reinterpret_cast<float*>(W + ws.route_w);
+  uint8_t* a_tiled = W + ws.a_tiled;
+  float* a_scale = reinterpret_cast<float*>(W + ws.a_scale);
+  uint8_t* c_hi = W + ws.c_hi;
+  uint8_t* c_lo = W + ws.c_lo;
+  float* c_scale = reinterpret_cast<float*>(W + ws.c_scale);
+  float* partial = reinterpret_cast<float*>(W + ws.partial);
+
+  if (int rc = cuda_check(cudaMemsetAsync(counts, 0, sizeof(int) * E_local, st), "memset counts")) return rc;
+  route_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, routed_scaling_factor, local_expert_offset,
+                                            E_local, topk_idx, topk_w, counts, token_nr);
+  dispatch_kernel<<<E_local, 1024, 0, st>>>(topk_idx, topk_w, counts, T, E_local, local_expert_offset,
+                                            n_tiles, tile_expert, tile_rows, route_token, route_w,
+                                            token_row);
+  gather_kernel<<<grid_for(static_cast<size_t>(ws.tiles_max) * TILE_M, 8, d->num_sms * 8), 256, 0, st>>>(
+      static_cast<const uint8_t*>(hidden), hidden_scale, T, n_tiles, ws.tiles_max, route_token, a_tiled,
+      a_scale);
+
+  Gemm1Args g1{a_tiled, a_scale, static_cast<const uint8_t*>(w13_packed), w13_scale, tile_expert,
+               n_tiles, ws.tiles_max, E_local, c_hi, c_lo, c_scale};
+  const int g1_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G1_NT, 1, d->num_sms);
+  gemm1_swiglu_kernel<<<g1_grid, G1_THREADS, G1_SMEM, st>>>(g1);
+
+  Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, tile_expert,
+               tile_rows, n_tiles, ws.tiles_max, E_local, route_w, partial};
+  const int g2_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G2_NT, 1, d->num_sms);
+  gemm2_weighted_kernel<<<g2_grid, G2_THREADS, G2_SMEM, st>>>(g2);
+
+  combine_kernel<<<T, 256, 0, st>>>(partial, token_nr, token_row, T,
+                                    static_cast<__nv_bfloat16*>(out_bf16));
+  return cuda_check(cudaGetLastError(), "moe_forward launch");
+}
+
+int moe_route(const float* logits, const float* bias, float routed_scaling_factor, int T,
+              int* topk_idx, float* topk_w, void* stream) {
+  if (T < 0) return fail(MOE_ERR_INVALID, "logits must be [T, 256]");
+  if (T == 0) return MOE_OK;
+  if (!logits || !bias || !topk_idx || !topk_w) return fail(MOE_ERR_INVALID, "moe_route: null pointer argument");
+  if (!aligned16(logits) || !aligned16(bias)) return fail(MOE_ERR_INVALID, "moe_route: logits and bias must be 16-byte aligned");
+  route_kernel<<<(T + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      logits, bias, T, routed_scaling_factor, 0, 0, topk_idx, topk_w, nullptr, nullptr);
+  return cuda_check(cudaGetLastError(), "route_kernel launch");
+}
+
+int moe_synth_logits(const float* table, uint64_t seed, int T, int E, float* out, void* stream) {
+  if (!table || !out || T < 0 || E < 0) return fail(MOE_ERR_INVALID, "moe_synth_logits: bad argument");
+  const long n = static_cast<long>(T) * E;
+  if (n == 0) return MOE_OK;
+  synth_logits_kernel<<<grid_for(static_cast<size_t>(n), 256, 4096), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      table, seed, n, out);
+  return cuda_check(cudaGetLastError(), "synth_logits launch");
+}
+
+int moe_synth_bias(const float* table, uint64_t seed, int E, float stddev, const int* hot_dev, int n_hot,
+                   float hot_value, uint16_t* out_bf16, void* stream) {
+  if (!table || !out_bf16 || E <= 0 || n_hot < 0 || (n_hot > 0 && !hot_dev))
+    return fail(MOE_ERR_INVALID, "moe_synth_bias: bad argument");
+  synth_bias_kernel<<<1, 256, 0, static_cast<cudaStream_t>(stream)>>>(table, seed, E, stddev, hot_dev, n_hot,
+                                                                       hot_value, out_bf16);
+  return cuda_check(cudaGetLastError(), "synth_bias launch");
+}
+
+int moe_synth_hidden(const float* table, uint64_t seed, int T, float stddev, void* hidden,
+                     float* hidden_scale, void* stream) {
+  if (!table || !hidden || !hidden_scale || T < 0) return fail(MOE_ERR_INVALID, "moe_synth_hidden: bad argument");
+  if (T == 0) return MOE_OK;
+  const size_t warps = static_cast<size_t>(T) * HB;
+  synth_hidden_kernel<<<grid_for(warps, 8, 8192), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      table, seed, T, stddev, static_cast<uint8_t*>(hidden), hidden_scale);
+  return cuda_check(cudaGetLastError(), "synth_hidden launch");
+}
+
+int moe_synth_w13(const float* table, uint64_t seed, int e0, int E, float stddev, void* w13,
+                  float* w13_scale, void* stream) {
+  if (!table || !w13 || !w13_scale || E <= 0 || e0 < 0) return fail(MOE_ERR_INVALID, "moe_synth_w13: bad argument");
+  const int blocks = E * (G1N / 128) * (H / 128);
+  synth_weight_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      table, seed, SYN_W13, e0, G1N, H, stddev, static_cast<uint8_t*>(w13), w13_scale);
+  return cuda_check(cudaGetLastError(), "synth_w13 launch");
+}
+
+int moe_synth_w2(const float* table, uint64_t seed, int e0, int E, float stddev, void* w2,
+                 float* w2_scale, void* stream) {
+  if (!table || !w2 || !w2_scale || E <= 0 || e0 < 0) return fail(MOE_ERR_INVALID, "moe_synth_w2: bad argument");
+  const int blocks = E * (H / 128) * (I / 128);
+  synth_weight_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      table, seed, SYN_W2, e0, H, I, stddev, static_cast<uint8_t*>(w2), w2_scale);
+  return cuda_check(cudaGetLastError(), "synth_w2 launch");
+}
+
+}  // extern "C"

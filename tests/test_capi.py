@@ -1,0 +1,82 @@
+"""The C ABI library loads without a GPU, exports every symbol include/moe_b200.h declares,
+and rejects bad arguments on the host (no device work is issued by these calls)."""
+import ctypes
+import os
+import re
+
+import pytest
+
+HEADER = os.path.join(os.path.dirname(os.path.dirname(__file__)), "include", "moe_b200.h")
+
+
+def declared_functions():
+    text = open(HEADER).read()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(moe_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_reference_entry_points():
+    names = declared_functions()
+    for n in ("moe_pack_w13", "moe_pack_w2", "moe_forward"):
+        assert n in names
+
+
+def test_library_exports_every_declared_symbol(pkg):
+    from importlib import import_module
+    native = import_module("15642_moe_b200._native")
+    lib = native.cuda_lib()
+    for name in declared_functions():
+        assert hasattr(lib, name), name
+        assert name in native.CUDA_SIGNATURES, name
+
+
+def test_sizes(pkg):
+    native = __import__("importlib").import_module("15642_moe_b200._native")
+    lib = native.cuda_lib()
+    assert lib.moe_pack_w13_bytes(32) == 32 * 4096 * 7168
+    assert lib.moe_pack_w2_bytes(32) == 32 * 7168 * 2048
+    assert lib.moe_pack_w13_bytes(0) == 0
+    ws = lib.moe_forward_workspace_bytes(64, 32)
+    assert ws > 0 and lib.moe_forward_workspace_bytes(4096, 32) > ws
+    lay = native.workspace_layout(64, 32)
+    assert lay["total"] == ws
+    offs = [v for k, v in lay.items()]
+    assert offs == sorted(offs) and all(v % 1024 == 0 for v in offs)
+    # worst case: every token routes all 8 picks to local experts, each tile padded
+    tiles = (64 * 8 + 32 * 127 + 127) // 128
+    assert lay["partial"] + tiles * 128 * 7168 * 4 <= lay["total"]
+
+
+def test_host_side_argument_errors(pkg):
+    native = __import__("importlib").import_module("15642_moe_b200._native")
+    lib = native.cuda_lib()
+    null = None
+    rc = lib.moe_forward(null, null, null, null, null, null, null, null, 1.0, 0, 16, 0, null, null, 0, null)
+    assert rc == 1 and b"E_local" in lib.moe_last_error()
+    rc = lib.moe_forward(null, null, null, null, null, null, null, null, 1.0, 0, -1, 32, null, null, 0, null)
+    assert rc == 1 and b"hidden must be [T, 7168]" in lib.moe_last_error()
+    # T == 0 is a no-op
+    assert lib.moe_forward(null, null, null, null, null, null, null, null, 1.0, 0, 0, 32, null, null, 0, null) == 0
+    rc = lib.moe_forward(null, null, null, null, null, null, null, null, 1.0, 0, 4, 32, null, null, 0, null)
+    assert rc == 1 and b"null" in lib.moe_last_error()
+    buf = (ctypes.c_uint8 * 64)()
+    p = ctypes.addressof(buf)
+    p16 = (p + 15) & ~15
+    rc = lib.moe_forward(p16, p16, p16, p16, p16, p16, p16, p16, 1.0, 0, 4, 32, p16, p16, 16, null)
+    assert rc == 3 and b"workspace too small" in lib.moe_last_error()
+    rc = lib.moe_forward(p16 + 1, p16, p16, p16, p16, p16, p16, p16, 1.0, 0, 4, 32, p16, p16, 16, null)
+    assert rc == 1 and b"aligned" in lib.moe_last_error()
+    assert lib.moe_pack_w13(null, 0, null, null) == 1
+    assert b"W13 must be [E_local, 4096, 7168]" in lib.moe_last_error()
+    assert lib.moe_pack_w2(null, 300, null, null) == 1
+
+
+def test_python_api_rejects_cpu_tensors(pkg):
+    import torch
+    w = torch.zeros((1, 4096, 7168), dtype=torch.float8_e4m3fn)
+    with pytest.raises(RuntimeError, match="CUDA tensor"):
+        pkg.pack_w13(w)
+    with pytest.raises(RuntimeError, match="W13 must be"):
+        pkg.pack_w13(torch.zeros((1, 4096, 7000), dtype=torch.float8_e4m3fn))
+    with pytest.raises(RuntimeError, match="FP8"):
+        pkg.pack_w2(torch.zeros((1, 7168, 2048), dtype=torch.float32))
