@@ -32,6 +32,9 @@ CUDA_SIGNATURES = {
     "moe_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                             c_void_p, c_float, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t,
                             c_void_p]),
+    "moe_forward_profiled": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                     c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_void_p,
+                                     c_void_p, c_size_t, c_void_p, c_void_p]),
     "moe_route": (c_int, [c_void_p, c_void_p, c_float, c_int, c_void_p, c_void_p, c_void_p]),
     "moe_workspace_layout": (c_int, [c_int, c_int, c_size_t_p, c_int]),
     "moe_synth_logits": (c_int, [c_void_p, c_uint64, c_int, c_int, c_void_p, c_void_p]),

@@ -152,11 +152,18 @@ int moe_workspace_layout(int T, int E_local, size_t* offsets, int n) {
   return 17;
 }
 
-int moe_forward(const void* hidden, const float* hidden_scale, const void* w13_packed,
-                const float* w13_scale, const void* w2_packed, const float* w2_scale,
-                const float* logits, const float* bias, float routed_scaling_factor,
-                int local_expert_offset, int T, int E_local, void* out_bf16, void* workspace,
-                size_t workspace_bytes, void* stream) {
+}  // extern "C"
+
+namespace {
+
+// The forward pipeline; when `events` is non-null, events[0..6] are recorded on the stream
+// before the first launch and after each of the six kernels (route, dispatch, gather, gemm1,
+// gemm2, combine).
+int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_packed,
+                 const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                 const float* logits, const float* bias, float routed_scaling_factor,
+                 int local_expert_offset, int T, int E_local, void* out_bf16, void* workspace,
+                 size_t workspace_bytes, void* stream, void* const* events) {
   if (T < 0) return fail(MOE_ERR_INVALID, "hidden must be [T, 7168]");
   if (E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "W13_packed must be [E_local, ...] with 1 <= E_local <= 256");
   if (T == 0) return MOE_OK;
@@ -191,29 +198,65 @@ int moe_forward(const void* hidden, const float* hidden_scale, const void* w13_p
   float* c_scale = reinterpret_cast<float*>(W + ws.c_scale);
   float* partial = reinterpret_cast<float*>(W + ws.partial);
 
+  auto mark = [&](int i) {
+    if (events != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
+  };
+  mark(0);
   if (int rc = cuda_check(cudaMemsetAsync(counts, 0, sizeof(int) * E_local, st), "memset counts")) return rc;
   route_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, routed_scaling_factor, local_expert_offset,
                                             E_local, topk_idx, topk_w, counts, token_nr);
+  mark(1);
   dispatch_kernel<<<E_local, 1024, 0, st>>>(topk_idx, topk_w, counts, T, E_local, local_expert_offset,
                                             n_tiles, tile_expert, tile_rows, route_token, route_w,
                                             token_row);
+  mark(2);
   gather_kernel<<<grid_for(static_cast<size_t>(ws.tiles_max) * TILE_M, 8, d->num_sms * 8), 256, 0, st>>>(
       static_cast<const uint8_t*>(hidden), hidden_scale, T, n_tiles, ws.tiles_max, route_token, a_tiled,
       a_scale);
+  mark(3);
 
   Gemm1Args g1{a_tiled, a_scale, static_cast<const uint8_t*>(w13_packed), w13_scale, tile_expert,
                n_tiles, ws.tiles_max, E_local, c_hi, c_lo, c_scale};
   const int g1_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G1_NT, 1, d->num_sms);
   gemm1_swiglu_kernel<<<g1_grid, G1_THREADS, G1_SMEM, st>>>(g1);
+  mark(4);
 
   Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, tile_expert,
                tile_rows, n_tiles, ws.tiles_max, E_local, route_w, partial};
   const int g2_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G2_NT, 1, d->num_sms);
   gemm2_weighted_kernel<<<g2_grid, G2_THREADS, G2_SMEM, st>>>(g2);
+  mark(5);
 
   combine_kernel<<<T, 256, 0, st>>>(partial, token_nr, token_row, T,
                                     static_cast<__nv_bfloat16*>(out_bf16));
+  mark(6);
   return cuda_check(cudaGetLastError(), "moe_forward launch");
+}
+
+}  // namespace
+
+extern "C" {
+
+int moe_forward(const void* hidden, const float* hidden_scale, const void* w13_packed,
+                const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                const float* logits, const float* bias, float routed_scaling_factor,
+                int local_expert_offset, int T, int E_local, void* out_bf16, void* workspace,
+                size_t workspace_bytes, void* stream) {
+  return forward_impl(hidden, hidden_scale, w13_packed, w13_scale, w2_packed, w2_scale, logits, bias,
+                      routed_scaling_factor, local_expert_offset, T, E_local, out_bf16, workspace,
+                      workspace_bytes, stream, nullptr);
+}
+
+int moe_forward_profiled(const void* hidden, const float* hidden_scale, const void* w13_packed,
+                         const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                         const float* logits, const float* bias, float routed_scaling_factor,
+                         int local_expert_offset, int T, int E_local, void* out_bf16,
+                         void* workspace, size_t workspace_bytes, void* stream,
+                         void* const* events) {
+  if (events == nullptr) return fail(MOE_ERR_INVALID, "moe_forward_profiled: events must not be null");
+  return forward_impl(hidden, hidden_scale, w13_packed, w13_scale, w2_packed, w2_scale, logits, bias,
+                      routed_scaling_factor, local_expert_offset, T, E_local, out_bf16, workspace,
+                      workspace_bytes, stream, events);
 }
 
 int moe_route(const float* logits, const float* bias, float routed_scaling_factor, int T,
@@ -228,9 +271,10 @@ int moe_route(const float* logits, const float* bias, float routed_scaling_facto
 }
 
 int moe_synth_logits(const float* table, uint64_t seed, int T, int E, float* out, void* stream) {
-  if (!table || !out || T < 0 || E < 0) return fail(MOE_ERR_INVALID, "moe_synth_logits: bad argument");
+  if (T < 0 || E < 0) return fail(MOE_ERR_INVALID, "moe_synth_logits: bad argument");
   const long n = static_cast<long>(T) * E;
   if (n == 0) return MOE_OK;
+  if (!table || !out) return fail(MOE_ERR_INVALID, "moe_synth_logits: bad argument");
   synth_logits_kernel<<<grid_for(static_cast<size_t>(n), 256, 4096), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       table, seed, n, out);
   return cuda_check(cudaGetLastError(), "synth_logits launch");
@@ -247,8 +291,9 @@ int moe_synth_bias(const float* table, uint64_t seed, int E, float stddev, const
 
 int moe_synth_hidden(const float* table, uint64_t seed, int T, float stddev, void* hidden,
                      float* hidden_scale, void* stream) {
-  if (!table || !hidden || !hidden_scale || T < 0) return fail(MOE_ERR_INVALID, "moe_synth_hidden: bad argument");
+  if (T < 0) return fail(MOE_ERR_INVALID, "moe_synth_hidden: bad argument");
   if (T == 0) return MOE_OK;
+  if (!table || !hidden || !hidden_scale) return fail(MOE_ERR_INVALID, "moe_synth_hidden: bad argument");
   const size_t warps = static_cast<size_t>(T) * HB;
   synth_hidden_kernel<<<grid_for(warps, 8, 8192), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       table, seed, T, stddev, static_cast<uint8_t*>(hidden), hidden_scale);

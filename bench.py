@@ -1,0 +1,458 @@
+#!/usr/bin/env python
+"""Benchmark of the B200 DeepSeek-V3/R1 FP8 MoE forward (one JSON line on rank 0).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload at N=1: benchmark configuration 2 (T=4096 tokens, 32 local experts of 256,
+local_expert_offset 0; the prefill case the headline tokens/s is quoted on). Each step is one
+full moe_forward: route -> dispatch -> gather -> GEMM1+SwiGLU -> GEMM2 -> combine. The
+1.41 GB of FP8 expert weights exceed the 126 MB L2, so no flush is needed between steps.
+The decode case (configuration 1, T=64) is reported alongside as microseconds per layer.
+
+Under torchrun (N > 1) every rank runs the same step on its own 32-expert slice of the
+256-expert layer (local_expert_offset = 32 * rank), without a data-path collective; the
+reported value is all ranks' tokens / max-over-ranks device time ("weak" scaling).
+
+--impl reference times the CPU restatement of reference/moe_ref.py (oracle/) on the host
+cores, on the same configuration (rank 0 only).
+"""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+import numpy as np
+import torch
+
+REPO = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, REPO)
+
+METRIC = "MoE fwd tokens/s @T=4096 (1-8 B200 EP); µs/layer @T=64; %HBM / %FP8 TC peak"
+W13_EXPERT_BYTES = 4096 * 7168
+W2_EXPERT_BYTES = 7168 * 2048
+W13_SCALE_BYTES = 32 * 56 * 4
+W2_SCALE_BYTES = 56 * 16 * 4
+FLOPS_G1_PER_ROUTE = 2 * 7168 * 4096
+FLOPS_G2_PER_ROUTE = 2 * 2048 * 7168
+STAGES = ["route", "dispatch", "gather", "gemm1_swiglu", "gemm2_weighted", "combine"]
+
+
+def load_peaks() -> dict:
+    path = os.path.join(REPO, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return dict(hbm_gbs=float(p["hbm_gbs"]), bf16_tflops=float(p["bf16_tflops"]), source="measured")
+    return dict(hbm_gbs=6650.0, bf16_tflops=1590.0, source="fallback")
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms in the background."""
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "200"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            self.proc.wait(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+        sm, smax, power, reasons = [], [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                smax.append(float(parts[2]))
+                power.append(float(parts[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        busy = [s for s, p in zip(sm, power) if p > 0.5 * max(power)] or sm
+        return {"sm_mhz": statistics.median(busy), "sm_max_mhz": max(smax),
+                "reasons": sorted(reasons), "samples": len(sm), "samples_under_load": len(busy),
+                "power_w_max": max(power)}
+
+
+def routing_stats(pkg, inp) -> dict:
+    idx, _ = pkg.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"])
+    idx = idx.cpu().numpy()
+    off, E = inp["local_expert_offset"], inp["gemm1_weights"].shape[0]
+    local = (idx >= off) & (idx < off + E)
+    counts = np.bincount((idx[local] - off).ravel(), minlength=E)
+    return dict(routes=int(local.sum()), active=int((counts > 0).sum()),
+                max_per_expert=int(counts.max()), tiles=int(((counts + 127) // 128).sum()))
+
+
+def kernel_work(rs: dict, T: int) -> dict:
+    """Algorithmic bytes and FLOPs per launch of each kernel (what it must move / compute)."""
+    r, a = rs["routes"], rs["active"]
+    return {
+        "gemm1_swiglu": dict(bytes=a * (W13_EXPERT_BYTES + W13_SCALE_BYTES) + r * (7168 + 56 * 4)
+                             + r * (2 * 2048 + 16 * 4), flops=r * FLOPS_G1_PER_ROUTE),
+        "gemm2_weighted": dict(bytes=a * (W2_EXPERT_BYTES + W2_SCALE_BYTES) + r * (2 * 2048 + 16 * 4)
+                               + r * 7168 * 4, flops=2 * r * FLOPS_G2_PER_ROUTE),
+        "gather": dict(bytes=r * (7168 + 56 * 4) * 2, flops=0),
+        "combine": dict(bytes=r * 7168 * 4 + T * 7168 * 2, flops=0),
+        "route": dict(bytes=T * 256 * 4 + T * 8 * 8, flops=0),
+        "dispatch": dict(bytes=T * 8 * 8, flops=0),
+    }
+
+
+class Step:
+    """One moe_forward of a fixed workload with resident packed weights and buffers."""
+
+    def __init__(self, pkg, inp, device):
+        self.pkg, self.inp, self.dev = pkg, inp, device
+        self.lib = pkg._native.cuda_lib()
+        self.T = inp["hidden_states"].shape[0]
+        self.E = inp["gemm1_weights"].shape[0]
+        self.w13p = pkg.pack_w13(inp["gemm1_weights"])
+        self.w2p = pkg.pack_w2(inp["gemm2_weights"])
+        self.hs = inp["hidden_states_scale"].float().contiguous()
+        self.s13 = inp["gemm1_weights_scale"].float().contiguous()
+        self.s2 = inp["gemm2_weights_scale"].float().contiguous()
+        self.lg = inp["routing_logits"].float().contiguous()
+        self.b = inp["routing_bias"].float().reshape(-1).contiguous()
+        self.out = torch.empty((self.T, 7168), dtype=torch.bfloat16, device=device)
+        self.ws = torch.empty(pkg.workspace_bytes(self.T, self.E), dtype=torch.uint8, device=device)
+        self.stream = torch.cuda.current_stream(device).cuda_stream
+        self.args = (inp["hidden_states"].data_ptr(), self.hs.data_ptr(), self.w13p.data_ptr(),
+                     self.s13.data_ptr(), self.w2p.data_ptr(), self.s2.data_ptr(), self.lg.data_ptr(),
+                     self.b.data_ptr(), float(inp["routed_scaling_factor"]),
+                     int(inp["local_expert_offset"]), self.T, self.E, self.out.data_ptr(),
+                     self.ws.data_ptr(), self.ws.numel(), self.stream)
+
+    def __call__(self):
+        self.pkg._native.check(self.lib.moe_forward(*self.args))
+
+    def profiled(self, events):
+        arr = (ctypes.c_void_p * 7)(*[e.cuda_event for e in events])
+        self.pkg._native.check(self.lib.moe_forward_profiled(*self.args, arr))
+
+
+def time_steps(fn, steps: int) -> float:
+    """Device time in ms of `steps` calls, CUDA events on the launching stream."""
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    s.record()
+    for _ in range(steps):
+        fn()
+    e.record()
+    torch.cuda.synchronize()
+    return s.elapsed_time(e)
+
+
+def stage_times(step: Step, reps: int) -> dict:
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(reps)]
+    for row in evs:          # torch creates the CUDA event on first record
+        for ev in row:
+            ev.record()
+    torch.cuda.synchronize()
+    for r in range(reps):
+        step.profiled(evs[r])
+    torch.cuda.synchronize()
+    out = {}
+    for i, name in enumerate(STAGES):
+        out[name] = statistics.mean(evs[r][i].elapsed_time(evs[r][i + 1]) for r in range(reps))
+    return out
+
+
+def roofline(stage_ms: dict, work: dict, peaks: dict, traffic: dict | None) -> dict:
+    dom = max(("gemm1_swiglu", "gemm2_weighted"), key=lambda k: stage_ms[k])
+    w, ms = work[dom], stage_ms[dom]
+    fp8_tflops = 2.0 * peaks["bf16_tflops"]          # dense FP8 issues at twice the bf16 rate
+    t_hbm = w["bytes"] / (peaks["hbm_gbs"] * 1e9)
+    t_tc = w["flops"] / (fp8_tflops * 1e12)
+    bound = "hbm" if t_hbm >= t_tc else "tensor"
+    if bound == "hbm":
+        achieved, peak, unit = w["bytes"] / (ms * 1e-3) / 1e9, peaks["hbm_gbs"], "GB/s"
+    else:
+        achieved, peak, unit = w["flops"] / (ms * 1e-3) / 1e12, fp8_tflops, "TFLOP/s"
+    tr = None
+    if traffic and dom in traffic:
+        tr = traffic[dom]
+    return {"kernel": dom, "bound": bound, "achieved": round(achieved, 1), "peak": peak,
+            "unit": unit, "frac": round(achieved / peak, 4), "traffic": tr,
+            "algorithmic_bytes": int(w["bytes"]), "algorithmic_flops": int(w["flops"]),
+            "kernel_us": round(ms * 1e3, 2), "peak_source": peaks["source"],
+            "tensor_frac_fp8": round(w["flops"] / (ms * 1e-3) / 1e12 / fp8_tflops, 4),
+            "hbm_frac": round(w["bytes"] / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)}
+
+
+def load_traffic(workload: str) -> dict | None:
+    path = os.path.join(REPO, "profiles", "traffic.json")
+    if not os.path.exists(path):
+        return None
+    with open(path) as f:
+        return json.load(f).get(workload)
+
+
+def e2e_run(pkg, inp, device, steps: int, warmup: int) -> dict:
+    """Public API (pkg.run) per step: H2D of the step's activations from pinned host memory,
+    the forward with resident weights, D2H of the bf16 result."""
+    host = {k: inp[k].cpu().pin_memory() for k in ("hidden_states", "hidden_states_scale", "routing_logits")}
+    dev = {k: torch.empty_like(inp[k]) for k in host}
+    out_host = torch.empty((inp["hidden_states"].shape[0], 7168), dtype=torch.bfloat16).pin_memory()
+    kw = dict(inp)
+
+    def one():
+        for k in host:
+            dev[k].copy_(host[k], non_blocking=True)
+        kw.update(dev)
+        out = pkg.run(**kw)
+        out_host.copy_(out, non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    ms = time_steps(one, steps)
+    h2d = sum(t.numel() * t.element_size() for t in host.values())
+    return {"ms_per_step": ms / steps, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size())}
+
+
+def cpu_oracle_time(pkg, inp, max_seconds: float, experts=None) -> tuple[float, str, int]:
+    """Seconds of one oracle layer (or of an expert sample scaled to the layer)."""
+    from oracle import moe_oracle as O
+    npi = O.to_numpy_inputs(inp)
+    rs_idx, _ = O.route(npi["routing_logits"], npi["routing_bias"], npi["routed_scaling_factor"])
+    off, E = npi["local_expert_offset"], npi["gemm1_weights"].shape[0]
+    active = [e for e in range(E) if (rs_idx == off + e).any()]
+    sample = active if experts is None else experts
+    O.moe_forward(**npi, experts=sample)        # first call pays the page faults; discarded
+    t0 = time.perf_counter()
+    O.moe_forward(**npi, experts=sample)
+    dt = time.perf_counter() - t0
+    scale = len(active) / max(1, len(sample))
+    desc = (f"full layer ({len(active)} active local experts)" if len(sample) == len(active)
+            else f"{len(sample)} of {len(active)} active local experts, time scaled x{scale:.2f}")
+    return dt * scale, desc, len(active)
+
+
+def make_workload(pkg, name: str, rank: int, device):
+    base = pkg.CONFIGS[2] if name == "prefill" else pkg.CONFIGS[1]
+    cfg = base.with_(local_expert_offset=32 * (rank % 8))
+    return cfg, pkg.make_inputs(cfg, device)
+
+
+def bench_ours(args, rank, world, local_rank, dist):
+    pkg = importlib.import_module("15642_moe_b200")
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    peaks = load_peaks()
+
+    cfg, inp = make_workload(pkg, "prefill", rank, device)
+    step = Step(pkg, inp, device)
+    rs = routing_stats(pkg, inp)
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    # Burn-in (untimed) so clocks settle and the sampler sees the GPU under this load.
+    sampler = ClockSampler(local_rank)
+    sampler.start()
+    t_end = time.time() + args.burn_in
+    while time.time() < t_end:
+        for _ in range(20):
+            step()
+        torch.cuda.synchronize()
+    if dist is not None:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ms = time_steps(step, args.steps)
+    if dist is not None:
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    clocks = sampler.stop()
+    status = pkg.device_status(reset=True)
+
+    stages = stage_times(step, min(args.steps, 50))
+    work = kernel_work(rs, cfg.T)
+    roof = roofline(stages, work, peaks, load_traffic("prefill_t4096"))
+
+    # Decode shape: microseconds per layer at T=64 (configuration 1).
+    dcfg, dinp = make_workload(pkg, "decode", rank, device)
+    dstep = Step(pkg, dinp, device)
+    drs = routing_stats(pkg, dinp)
+    for _ in range(max(args.warmup, 3)):
+        dstep()
+    dms = time_steps(dstep, max(args.steps, 20)) / max(args.steps, 20)
+    dstages = stage_times(dstep, 20)
+    droof = roofline(dstages, kernel_work(drs, dcfg.T), peaks, load_traffic("decode_t64"))
+    layer_bytes = drs["active"] * (W13_EXPERT_BYTES + W2_EXPERT_BYTES + W13_SCALE_BYTES + W2_SCALE_BYTES)
+
+    e2e = e2e_run(pkg, inp, device, args.steps, args.warmup)
+    if dist is not None:
+        t = torch.tensor([e2e["ms_per_step"]], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e["ms_per_step"] = float(t.item())
+
+    if rank != 0:
+        return None
+    tokens = cfg.T * world
+    line = {
+        "metric": METRIC,
+        "value": round(tokens * args.steps / (ms * 1e-3), 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3 (fp32 accumulate)",
+        "data": "synthetic: seeded N(0,1) logits/hidden, N(0,0.1) bias, N(0,0.02) weights, "
+                "e4m3 with amax/448 128-block scales",
+        "config": {"workload": "config2_prefill_t4096", "T": cfg.T, "E_local": cfg.E_local,
+                   "experts_total": 256, "local_expert_offset": "32*rank",
+                   "routed_scaling_factor": cfg.routed_scaling_factor, "seed": cfg.seed,
+                   "routes": rs["routes"], "active_experts": rs["active"],
+                   "max_routes_per_expert": rs["max_per_expert"], "tiles": rs["tiles"],
+                   "parallelism": f"{world} x independent 32-expert slices" if world > 1 else "1 GPU",
+                   "l2": "inputs larger than L2 (1.41 GB FP8 expert weights per step)"},
+        "roofline": roof,
+        "stage_us": {k: round(v * 1e3, 2) for k, v in stages.items()},
+        "decode_t64": {"us_per_layer": round(dms * 1e3, 2), "routes": drs["routes"],
+                       "active_experts": drs["active"],
+                       "weight_bytes": int(layer_bytes),
+                       "hbm_frac_layer": round(layer_bytes / (dms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                       "roofline": droof, "stage_us": {k: round(v * 1e3, 2) for k, v in dstages.items()}},
+        "e2e": {"value": round(cfg.T * world / (e2e["ms_per_step"] * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
+                "ms_per_step": round(e2e["ms_per_step"], 4)},
+        "gpu_launches": 6 * args.steps,
+        "clocks": clocks,
+        "device_status": status,
+    }
+    if world == 1 and not args.no_cpu_baseline:
+        secs, desc, _ = cpu_oracle_time(pkg, {k: (v.cpu() if isinstance(v, torch.Tensor) else v)
+                                              for k, v in inp.items()}, 30.0)
+        line["cpu_baseline"] = {"value": round(cfg.T / secs, 2), "unit": "tokens/s",
+                                "cores": os.cpu_count(), "kind": "port",
+                                "sample": f"oracle/moe_oracle.py (numpy restatement of "
+                                          f"reference/moe_ref.py), T={cfg.T}, {desc}, "
+                                          f"1 warm call after 1 discarded call"}
+    return line
+
+
+def bench_reference(args, rank):
+    """CPU restatement of the reference (oracle/) on the host cores, same config / metric."""
+    if rank != 0:
+        return None
+    pkg = importlib.import_module("15642_moe_b200")
+    cfg = pkg.CONFIGS[2]
+    inp = pkg.make_inputs(cfg, "cuda:0" if torch.cuda.is_available() else "cpu")
+    inp = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
+    from oracle import moe_oracle as O
+    npi = O.to_numpy_inputs(inp)
+    idx, _ = O.route(npi["routing_logits"], npi["routing_bias"], npi["routed_scaling_factor"])
+    active = [e for e in range(32) if (idx == e).any()]
+    # First warm-up call on the full layer sizes the per-step sample so the run stays bounded.
+    t0 = time.perf_counter()
+    O.moe_forward(**npi, experts=active[:2])
+    per_expert = (time.perf_counter() - t0) / 2
+    budget = 150.0 / max(1, args.steps + args.warmup)
+    n_s = int(max(1, min(len(active), budget // max(per_expert, 1e-3))))
+    times = []
+    for i in range(args.warmup + args.steps):
+        sample = [active[(i * n_s + j) % len(active)] for j in range(n_s)]
+        t0 = time.perf_counter()
+        O.moe_forward(**npi, experts=sample)
+        dt = (time.perf_counter() - t0) * len(active) / n_s
+        if i >= args.warmup:
+            times.append(dt)
+    secs = statistics.mean(times)
+    value = cfg.T / secs
+    sample_desc = (f"per step {n_s} of {len(active)} active local experts (rotating), full routing, "
+                   f"time scaled x{len(active) / n_s:.2f}; oracle/moe_oracle.py numpy restatement of "
+                   f"reference/moe_ref.py")
+    return {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "impl": "reference",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(secs * 1e3, 2), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f32", "data": "synthetic (same generator and seed)",
+            "config": {"workload": "config2_prefill_t4096", "T": cfg.T, "E_local": 32},
+            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": os.cpu_count(),
+                             "kind": "port", "sample": sample_desc},
+            "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=50)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--burn-in", type=float, default=2.0, help="untimed seconds before timing")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        line = bench_reference(args, rank)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+        return
+
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as tdist
+        torch.cuda.set_device(local_rank)
+        tdist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                 device_id=torch.device("cuda", local_rank))
+        dist = tdist
+    try:
+        line = bench_ours(args, rank, world, local_rank, dist)
+        if line is not None:
+            print(json.dumps(line), flush=True)
+    finally:
+        if dist is not None:
+            dist.barrier()
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -79,6 +79,16 @@ int moe_forward(const void* hidden, const float* hidden_scale, const void* w13_p
                 int local_expert_offset, int T, int E_local, void* out_bf16, void* workspace,
                 size_t workspace_bytes, void* stream);
 
+/* moe_forward that also records events[0..6] (cudaEvent_t) on `stream`: before the first
+ * launch and after each of its six kernels (route, dispatch, gather, gemm1, gemm2,
+ * combine), for per-kernel timing. No reference counterpart (instrumentation only). */
+int moe_forward_profiled(const void* hidden, const float* hidden_scale, const void* w13_packed,
+                         const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                         const float* logits, const float* bias, float routed_scaling_factor,
+                         int local_expert_offset, int T, int E_local, void* out_bf16,
+                         void* workspace, size_t workspace_bytes, void* stream,
+                         void* const* events);
+
 /* Router alone (the routing half of moe_forward, reference/moe_ref.py:82-107): writes the
  * 8 selected global experts per token in selection order (descending biased score, ties to
  * the lower index) and their weights. No reference counterpart as a separate entry: the

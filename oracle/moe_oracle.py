@@ -19,6 +19,9 @@ The routing weight sum runs in ascending expert order (moe_ref.py:105 sums a den
 """
 from __future__ import annotations
 
+import os
+from concurrent.futures import ThreadPoolExecutor
+
 import numpy as np
 
 H = 7168
@@ -29,6 +32,10 @@ GROUP_SIZE = 32
 TOP_K = 8
 TOPK_GROUP = 4
 BLOCK = 128
+
+
+def _threads() -> int:
+    return max(1, min(16, os.cpu_count() or 1))
 
 
 # ---------------------------------------------------------------------------- number formats
@@ -110,11 +117,16 @@ def dequant_hidden(hidden_u8: np.ndarray, hidden_scale: np.ndarray) -> np.ndarra
     return (a * np.asarray(hidden_scale, np.float32).T[:, :, None]).reshape(T, H).astype(np.float32)
 
 
-def dequant_block(w_u8: np.ndarray, scale: np.ndarray) -> np.ndarray:
-    """W = fp8(w) * S[r/128, c/128] for one expert matrix (moe_ref.py:69-79)."""
+def dequant_block(w_u8: np.ndarray, scale: np.ndarray, out: np.ndarray | None = None) -> np.ndarray:
+    """W = fp8(w) * S[r/128, c/128] for one expert matrix (moe_ref.py:69-79), written in place
+    into ``out`` when given (no temporaries: the CPU cost of this step is memory traffic)."""
     R, C = w_u8.shape
-    w = decode_e4m3(w_u8).reshape(R // BLOCK, BLOCK, C // BLOCK, BLOCK)
-    return (w * np.asarray(scale, np.float32)[:, None, :, None]).reshape(R, C).astype(np.float32)
+    if out is None:
+        out = np.empty((R, C), np.float32)
+    np.take(E4M3, np.asarray(w_u8, np.uint8), out=out)
+    o4 = out.reshape(R // BLOCK, BLOCK, C // BLOCK, BLOCK)
+    np.multiply(o4, np.asarray(scale, np.float32)[:, None, :, None], out=o4)
+    return out
 
 
 def expert_rows(topk_idx: np.ndarray, ge: int) -> np.ndarray:
@@ -142,23 +154,38 @@ def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale
     topk_idx, topk_w = route(logits, routing_bias, routed_scaling_factor)
     A = dequant_hidden(hidden_states, hidden_states_scale)
     out = np.zeros((T, H), np.float32)                       # moe_ref.py:110
+    work = []
     for le in (range(E_local) if experts is None else experts):
         ge = int(local_expert_offset) + le
         if ge < 0 or ge >= E_GLOBAL:                         # moe_ref.py:115-116
             continue
         tok = expert_rows(topk_idx, ge)
-        if tok.size == 0:
-            continue
-        W13 = dequant_block(gemm1_weights[le], gemm1_weights_scale[le])
-        G1 = A[tok] @ W13.T                                  # moe_ref.py:128
-        del W13
-        X1, X2 = G1[:, :I], G1[:, I:]                        # moe_ref.py:129
-        C = ((X2 / (np.float32(1.0) + np.exp(-X2))) * X1).astype(np.float32)  # :130
-        W2 = dequant_block(gemm2_weights[le], gemm2_weights_scale[le])
-        O = C @ W2.T                                         # moe_ref.py:131
-        del W2
-        w_tok = topk_w[tok][topk_idx[tok] == ge]             # moe_ref.py:133
-        out[tok] += (O * w_tok[:, None]).astype(np.float32)  # moe_ref.py:134
+        if tok.size:
+            work.append((le, ge, tok))
+
+    # The fp32 dequantisation of moe_ref.py:69-79 is elementwise; numpy runs it on one core,
+    # so experts are dequantised on a thread pool (numpy releases the GIL) a batch at a time,
+    # into per-worker buffers reused across batches.
+    batch = max(1, min(len(work), _threads()))
+    bufs = [(np.empty((2 * I, H), np.float32), np.empty((H, I), np.float32)) for _ in range(batch)]
+
+    def deq(slot_le):
+        slot, le = slot_le
+        return (dequant_block(gemm1_weights[le], gemm1_weights_scale[le], bufs[slot][0]),
+                dequant_block(gemm2_weights[le], gemm2_weights_scale[le], bufs[slot][1]))
+
+    with ThreadPoolExecutor(max_workers=batch) as ex:
+        for b0 in range(0, len(work), batch):
+            chunk = work[b0:b0 + batch]
+            weights = list(ex.map(deq, [(i, le) for i, (le, _, _) in enumerate(chunk)]))
+            for (le, ge, tok), (W13, W2) in zip(chunk, weights):
+                G1 = A[tok] @ W13.T                          # moe_ref.py:128
+                X1, X2 = G1[:, :I], G1[:, I:]                # moe_ref.py:129
+                C = ((X2 / (np.float32(1.0) + np.exp(-X2))) * X1).astype(np.float32)  # :130
+                O = C @ W2.T                                 # moe_ref.py:131
+                w_tok = topk_w[tok][topk_idx[tok] == ge]     # moe_ref.py:133
+                out[tok] += (O * w_tok[:, None]).astype(np.float32)  # moe_ref.py:134
+            del weights
     res = out if return_fp32 else f32_to_bf16_bits(out)      # moe_ref.py:136
     if return_routing:
         return res, topk_idx, topk_w
