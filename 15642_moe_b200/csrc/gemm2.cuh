@@ -25,11 +25,12 @@ struct Gemm2Args {
   const float* w2_scale;    // [E, 56, 16]
   const int* tile_expert;   // [tiles]
   const int* tile_rows;     // [tiles]
+  const int* tile_dense;    // [tiles]  dense route index of the tile's first row
   const int* n_tiles;       // [1]
   int tiles_max;            // capacity of the workspace tile arrays
   int E_local;              // number of local experts (bounds of tile_expert)
   const float* route_w;     // [tiles * 128]
-  float* partial;           // [tiles * 128, 7168]
+  float* partial;           // [routes, 7168]
 };
 
 constexpr int G2_STAGES = 3;
@@ -204,7 +205,7 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(Gemm2Args
       if (row < p.tile_rows[tile]) {
         const float w = p.route_w[static_cast<size_t>(tile) * TILE_M + row];
         float4* dst = reinterpret_cast<float4*>(p.partial +
-                                                (static_cast<size_t>(tile) * TILE_M + row) * H +
+                                                static_cast<size_t>(p.tile_dense[tile] + row) * H +
                                                 nt * 256 + hf * 128);
 #pragma unroll
         for (int i = 0; i < 32; ++i)

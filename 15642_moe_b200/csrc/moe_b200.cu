@@ -145,11 +145,12 @@ size_t moe_forward_workspace_bytes(int T, int E_local) {
 int moe_workspace_layout(int T, int E_local, size_t* offsets, int n) {
   if (T < 0 || E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "bad T or E_local");
   const Workspace w = make_workspace(T, E_local);
-  const size_t v[17] = {w.counts,      w.n_tiles,   w.topk_idx,    w.topk_w,  w.token_nr, w.token_row,
-                        w.tile_expert, w.tile_rows, w.route_token, w.route_w, w.a_tiled,  w.a_scale,
-                        w.c_hi,        w.c_lo,      w.c_scale,     w.partial, w.total};
-  for (int i = 0; i < n && i < 17; ++i) offsets[i] = v[i];
-  return 17;
+  const size_t v[18] = {w.counts,     w.n_tiles,     w.topk_idx,    w.topk_w,  w.token_nr,
+                        w.token_row,  w.tile_expert, w.tile_rows,   w.tile_dense, w.route_token,
+                        w.route_w,    w.a_tiled,     w.a_scale,     w.c_hi,    w.c_lo,
+                        w.c_scale,    w.partial,     w.total};
+  for (int i = 0; i < n && i < 18; ++i) offsets[i] = v[i];
+  return 18;
 }
 
 }  // extern "C"
@@ -189,6 +190,7 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   int* token_row = reinterpret_cast<int*>(W + ws.token_row);
   int* tile_expert = reinterpret_cast<int*>(W + ws.tile_expert);
   int* tile_rows = reinterpret_cast<int*>(W + ws.tile_rows);
+  int* tile_dense = reinterpret_cast<int*>(W + ws.tile_dense);
   int* route_token = reinterpret_cast<int*>(W + ws.route_token);
   float* route_w = reinterpret_cast<float*>(W + ws.route_w);
   uint8_t* a_tiled = W + ws.a_tiled;
@@ -207,8 +209,8 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
                                             E_local, topk_idx, topk_w, counts, token_nr);
   mark(1);
   dispatch_kernel<<<E_local, 1024, 0, st>>>(topk_idx, topk_w, counts, T, E_local, local_expert_offset,
-                                            n_tiles, tile_expert, tile_rows, route_token, route_w,
-                                            token_row);
+                                            n_tiles, tile_expert, tile_rows, tile_dense, route_token,
+                                            route_w, token_row);
   mark(2);
   gather_kernel<<<grid_for(static_cast<size_t>(ws.tiles_max) * TILE_M, 8, d->num_sms * 8), 256, 0, st>>>(
       static_cast<const uint8_t*>(hidden), hidden_scale, T, n_tiles, ws.tiles_max, route_token, a_tiled,
@@ -222,12 +224,12 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   mark(4);
 
   Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, tile_expert,
-               tile_rows, n_tiles, ws.tiles_max, E_local, route_w, partial};
+               tile_rows, tile_dense, n_tiles, ws.tiles_max, E_local, route_w, partial};
   const int g2_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G2_NT, 1, d->num_sms);
   gemm2_weighted_kernel<<<g2_grid, G2_THREADS, G2_SMEM, st>>>(g2);
   mark(5);
 
-  combine_kernel<<<T, 256, 0, st>>>(partial, token_nr, token_row, T,
+  combine_kernel<<<T, COMBINE_THREADS, 0, st>>>(partial, token_nr, token_row, T,
                                     static_cast<__nv_bfloat16*>(out_bf16));
   mark(6);
   return cuda_check(cudaGetLastError(), "moe_forward launch");

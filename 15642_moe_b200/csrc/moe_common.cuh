@@ -320,6 +320,7 @@ struct Workspace {
   size_t token_row;    // int32 [T, 8]                 routed row of each local route
   size_t tile_expert;  // int32 [tiles_max]            local expert of each tile
   size_t tile_rows;    // int32 [tiles_max]            valid rows of each tile
+  size_t tile_dense;   // int32 [tiles_max]            dense route index of each tile's row 0
   size_t route_token;  // int32 [tiles_max*128]        token of each routed row (-1 = pad)
   size_t route_w;      // fp32  [tiles_max*128]        routing weight of each routed row
   size_t a_tiled;      // u8    [tiles_max, 56, 128, 128] gathered hidden rows, SW128 tiles
@@ -327,7 +328,7 @@ struct Workspace {
   size_t c_hi;         // u8    [tiles_max, 16, 128, 128] SwiGLU output, e4m3 high part
   size_t c_lo;         // u8    [tiles_max, 16, 128, 128] e4m3 residual
   size_t c_scale;      // fp32  [tiles_max, 16, 128]   per (row, 128-block) scale
-  size_t partial;      // fp32  [tiles_max*128, 7168]  weighted expert outputs
+  size_t partial;      // fp32  [routes_max, 7168]     weighted expert output per local route
   size_t total;
   int tiles_max;
 };
@@ -336,8 +337,12 @@ __host__ __device__ inline size_t ws_align(size_t x) { return (x + 1023) & ~stat
 
 inline Workspace make_workspace(int T, int E_local) {
   Workspace w{};
+  // Tiles: each active expert pads its rows up to a multiple of 128, and there are at most
+  // min(E_local, routes) active experts.
   int kmax = E_local < TOP_K ? E_local : TOP_K;
-  long long rows = static_cast<long long>(T) * kmax + static_cast<long long>(E_local) * (TILE_M - 1);
+  long long routes = static_cast<long long>(T) * kmax;
+  long long active = routes < E_local ? routes : E_local;
+  long long rows = routes + active * (TILE_M - 1);
   w.tiles_max = static_cast<int>((rows + TILE_M - 1) / TILE_M);
   size_t tiles = static_cast<size_t>(w.tiles_max);
   size_t off = 0;
@@ -354,6 +359,7 @@ inline Workspace make_workspace(int T, int E_local) {
   w.token_row = take(sizeof(int) * TOP_K * static_cast<size_t>(T));
   w.tile_expert = take(sizeof(int) * tiles);
   w.tile_rows = take(sizeof(int) * tiles);
+  w.tile_dense = take(sizeof(int) * tiles);
   w.route_token = take(sizeof(int) * tiles * TILE_M);
   w.route_w = take(sizeof(float) * tiles * TILE_M);
   w.a_tiled = take(tiles * HB * TILE_BYTES);
@@ -361,7 +367,7 @@ inline Workspace make_workspace(int T, int E_local) {
   w.c_hi = take(tiles * IB * TILE_BYTES);
   w.c_lo = take(tiles * IB * TILE_BYTES);
   w.c_scale = take(sizeof(float) * tiles * IB * TILE_M);
-  w.partial = take(sizeof(float) * tiles * TILE_M * H);
+  w.partial = take(sizeof(float) * static_cast<size_t>(T) * kmax * H);
   w.total = off;
   return w;
 }

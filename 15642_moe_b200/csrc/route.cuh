@@ -123,16 +123,21 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
 
   // Weights: unbiased scores renormalised over the 8 picks, times the scaling factor
   // (moe_ref.py:103-107). The sum runs in ascending expert order.
+  int rank_of[TOP_K];
+#pragma unroll
+  for (int k = 0; k < TOP_K; ++k) {
+    int rk = 0;
+#pragma unroll
+    for (int j = 0; j < TOP_K; ++j) rk += sel_idx[j] < sel_idx[k] ? 1 : 0;
+    rank_of[k] = rk;
+  }
   float wsum = 0.0f;
 #pragma unroll
   for (int r = 0; r < TOP_K; ++r) {
+    float v = 0.0f;
 #pragma unroll
-    for (int k = 0; k < TOP_K; ++k) {
-      int rk = 0;
-#pragma unroll
-      for (int j = 0; j < TOP_K; ++j) rk += sel_idx[j] < sel_idx[k] ? 1 : 0;
-      if (rk == r) wsum = __fadd_rn(wsum, sel_s[k]);
-    }
+    for (int k = 0; k < TOP_K; ++k) v = rank_of[k] == r ? sel_s[k] : v;
+    wsum = __fadd_rn(wsum, v);
   }
   wsum = __fadd_rn(wsum, 1e-20f);
 
@@ -152,29 +157,38 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
 }
 
 // One CTA per local expert: finds the expert's tokens in token order and lays them out as
-// routed rows of its 128-row tiles. Tile offsets come from the per-expert counts.
+// routed rows of its 128-row tiles. Tile offsets and the dense row base (index of the expert's
+// first route among all local routes, used for the expert-output rows) come from the counts.
 __global__ void __launch_bounds__(1024) dispatch_kernel(
     const int* __restrict__ topk_idx, const float* __restrict__ topk_w,
     const int* __restrict__ counts, int T, int E_local, int local_offset, int* __restrict__ n_tiles,
-    int* __restrict__ tile_expert, int* __restrict__ tile_rows, int* __restrict__ route_token,
-    float* __restrict__ route_w, int* __restrict__ token_row) {
-  __shared__ int s_off, s_running, s_total;
+    int* __restrict__ tile_expert, int* __restrict__ tile_rows, int* __restrict__ tile_dense,
+    int* __restrict__ route_token, float* __restrict__ route_w, int* __restrict__ token_row) {
+  __shared__ int s_cnt[E_GLOBAL];
+  __shared__ int s_off, s_base, s_running, s_total;
   __shared__ int warp_pre[32];
   const int e = blockIdx.x;
   const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+  if (tid < E_local) s_cnt[tid] = counts[tid];
+  __syncthreads();
   if (tid == 0) {
-    int off = 0;
-    for (int i = 0; i < e; ++i) off += (counts[i] + TILE_M - 1) / TILE_M;
+    int off = 0, base = 0;
+    for (int i = 0; i < e; ++i) {
+      off += (s_cnt[i] + TILE_M - 1) / TILE_M;
+      base += s_cnt[i];
+    }
     s_off = off;
+    s_base = base;
     s_running = 0;
-    if (e == E_local - 1) *n_tiles = off + (counts[e] + TILE_M - 1) / TILE_M;
+    if (e == E_local - 1) *n_tiles = off + (s_cnt[e] + TILE_M - 1) / TILE_M;
   }
   __syncthreads();
-  const int off = s_off, cnt = counts[e];
+  const int off = s_off, cnt = s_cnt[e], dense0 = s_base;
   const int nt = (cnt + TILE_M - 1) / TILE_M;
   for (int i = tid; i < nt; i += blockDim.x) {
     tile_expert[off + i] = e;
     tile_rows[off + i] = min(TILE_M, cnt - TILE_M * i);
+    tile_dense[off + i] = dense0 + TILE_M * i;
   }
   const int ge = local_offset + e;
   const size_t row0 = static_cast<size_t>(off) * TILE_M;
@@ -217,7 +231,7 @@ __global__ void __launch_bounds__(1024) dispatch_kernel(
         const size_t row = row0 + slot;
         route_token[row] = t;
         route_w[row] = w;
-        token_row[static_cast<size_t>(t) * TOP_K + kslot] = static_cast<int>(row);
+        token_row[static_cast<size_t>(t) * TOP_K + kslot] = dense0 + slot;
       } else {
         report_status(ST_BAD_INDEX);
       }
@@ -264,37 +278,56 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__
   }
 }
 
+constexpr int COMBINE_THREADS = H / 16;  // 448: each thread owns 16 consecutive columns
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
 // One CTA per token: out[t] = bf16( sum over its local routes, ascending expert order,
 // of the weighted expert outputs ), starting from +0 like the reference's zero tensor.
-__global__ void __launch_bounds__(256) combine_kernel(const float* __restrict__ partial,
-                                                      const int* __restrict__ token_nr,
-                                                      const int* __restrict__ token_row, int T,
-                                                      __nv_bfloat16* __restrict__ out) {
+__global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(const float* __restrict__ partial,
+                                                                  const int* __restrict__ token_nr,
+                                                                  const int* __restrict__ token_row,
+                                                                  int T,
+                                                                  __nv_bfloat16* __restrict__ out) {
   const int t = blockIdx.x;
   if (t >= T) return;
   const int n = token_nr[t];
-  int rows[TOP_K];
+  const int c0 = threadIdx.x * 16;
+  float acc[16];
 #pragma unroll
-  for (int k = 0; k < TOP_K; ++k) rows[k] = k < n ? token_row[static_cast<size_t>(t) * TOP_K + k] : 0;
-  for (int q = threadIdx.x; q < H / 4; q += blockDim.x) {
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
 #pragma unroll
-    for (int k = 0; k < TOP_K; ++k) {
-      if (k < n) {
-        float4 p = __ldg(reinterpret_cast<const float4*>(partial + static_cast<size_t>(rows[k]) * H) + q);
-        acc.x = __fadd_rn(acc.x, p.x);
-        acc.y = __fadd_rn(acc.y, p.y);
-        acc.z = __fadd_rn(acc.z, p.z);
-        acc.w = __fadd_rn(acc.w, p.w);
+  for (int k = 0; k < TOP_K; ++k) {
+    if (k < n) {
+      const float4* src = reinterpret_cast<const float4*>(
+          partial + static_cast<size_t>(token_row[static_cast<size_t>(t) * TOP_K + k]) * H + c0);
+      float4 p[4];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) p[j] = __ldcs(src + j);
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        acc[4 * j + 0] = __fadd_rn(acc[4 * j + 0], p[j].x);
+        acc[4 * j + 1] = __fadd_rn(acc[4 * j + 1], p[j].y);
+        acc[4 * j + 2] = __fadd_rn(acc[4 * j + 2], p[j].z);
+        acc[4 * j + 3] = __fadd_rn(acc[4 * j + 3], p[j].w);
       }
     }
-    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y);
-    __nv_bfloat162 hi = __floats2bfloat162_rn(acc.z, acc.w);
-    uint2 pk;
-    pk.x = *reinterpret_cast<uint32_t*>(&lo);
-    pk.y = *reinterpret_cast<uint32_t*>(&hi);
-    *reinterpret_cast<uint2*>(out + static_cast<size_t>(t) * H + q * 4) = pk;
   }
+  uint4 o0, o1;
+  o0.x = pack_bf16x2(acc[0], acc[1]);
+  o0.y = pack_bf16x2(acc[2], acc[3]);
+  o0.z = pack_bf16x2(acc[4], acc[5]);
+  o0.w = pack_bf16x2(acc[6], acc[7]);
+  o1.x = pack_bf16x2(acc[8], acc[9]);
+  o1.y = pack_bf16x2(acc[10], acc[11]);
+  o1.z = pack_bf16x2(acc[12], acc[13]);
+  o1.w = pack_bf16x2(acc[14], acc[15]);
+  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + c0);
+  dst[0] = o0;
+  dst[1] = o1;
 }
 
 }  // namespace moe

@@ -98,8 +98,8 @@ int moe_route(const float* logits, const float* bias, float routed_scaling_facto
 
 /* Byte offsets of the internal workspace regions for (T, E_local), in this order:
  * counts, n_tiles, topk_idx, topk_w, token_nr, token_row, tile_expert, tile_rows,
- * route_token, route_w, a_tiled, a_scale, c_hi, c_lo, c_scale, partial, total.
- * Writes min(n, 17) values; returns the number of regions (17). For tests and tooling. */
+ * tile_dense, route_token, route_w, a_tiled, a_scale, c_hi, c_lo, c_scale, partial, total.
+ * Writes min(n, 18) values; returns the number of regions (18). For tests and tooling. */
 int moe_workspace_layout(int T, int E_local, size_t* offsets, int n);
 
 /* ---- Seeded synthetic inputs on the GPU (bit-identical to the CPU generator) ----

@@ -128,7 +128,10 @@ def test_stages(pkg, oracle):
     cs = region(ws, lay, "c_scale", torch.float32, n_tiles * 16 * 128).reshape(n_tiles, 16, 128)
     cval = (oracle.decode_e4m3(hi) + oracle.decode_e4m3(lo)) * cs[..., None]
     cval = cval.transpose(0, 2, 1, 3).reshape(n_tiles * 128, 2048)
-    partial = region(ws, lay, "partial", torch.float32, n_tiles * 128 * 7168).reshape(n_tiles * 128, 7168)
+    routes = int(exp_counts.sum())
+    partial = region(ws, lay, "partial", torch.float32, routes * 7168).reshape(routes, 7168)
+    tile_dense = region(ws, lay, "tile_dense", torch.int32, n_tiles)
+    dense_base = np.concatenate([[0], np.cumsum(exp_counts)[:-1]])
     t0 = 0
     worst_c, worst_o = 0.0, 0.0
     for e in range(E):
@@ -136,6 +139,8 @@ def test_stages(pkg, oracle):
         if nt == 0:
             continue
         rows = np.arange(t0 * 128, t0 * 128 + exp_counts[e])
+        drows = dense_base[e] + np.arange(exp_counts[e])
+        assert tile_dense[t0] == dense_base[e]
         toks = route_token[rows]
         W13 = oracle.dequant_block(npi["gemm1_weights"][e], npi["gemm1_weights_scale"][e])
         G1 = A[toks] @ W13.T
@@ -145,7 +150,7 @@ def test_stages(pkg, oracle):
         worst_c = max(worst_c, float(err.max()))
         W2 = oracle.dequant_block(npi["gemm2_weights"][e], npi["gemm2_weights_scale"][e])
         Oe = (C @ W2.T) * route_w[rows][:, None]
-        rel = np.abs(partial[rows] - Oe).max(axis=1) / (np.abs(Oe).max(axis=1) + 1e-30)
+        rel = np.abs(partial[drows] - Oe).max(axis=1) / (np.abs(Oe).max(axis=1) + 1e-30)
         worst_o = max(worst_o, float(rel.max()))
         t0 += nt
     print("worst C block-relative err", worst_c, "worst partial row-relative err", worst_o)
