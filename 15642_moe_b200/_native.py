@@ -32,6 +32,9 @@ CUDA_SIGNATURES = {
     "moe_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                             c_void_p, c_float, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t,
                             c_void_p]),
+    "moe_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                    c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_void_p,
+                                    c_void_p]),
     "moe_forward_profiled": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                      c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_void_p,
                                      c_void_p, c_size_t, c_void_p, c_void_p]),

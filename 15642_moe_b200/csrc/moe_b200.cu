@@ -38,9 +38,17 @@ int cuda_check(cudaError_t e, const char* what) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+// Scratch of moe_forward_noalloc, for callers that cannot allocate device memory. One copy
+// per device that loads this library, held until the process exits. Host code may not use the
+// array's name as a device address: the address comes from cudaGetSymbolAddress, taken once
+// per device with that device current (see noalloc_scratch()).
+constexpr size_t NOALLOC_SCRATCH_BYTES = static_cast<size_t>(MOE_NOALLOC_SCRATCH_BYTES);
+static __device__ __align__(256) uint8_t g_noalloc_scratch[NOALLOC_SCRATCH_BYTES];
+
 struct DeviceInfo {
   bool ready = false;
   int num_sms = 0;
+  void* noalloc_scratch = nullptr;  // device address of g_noalloc_scratch on this device
 };
 std::mutex g_dev_mu;
 DeviceInfo g_dev[64];
@@ -76,6 +84,19 @@ int device_info(DeviceInfo** out) {
     d.ready = true;
   }
   *out = &d;
+  return MOE_OK;
+}
+
+// Device address of this device's g_noalloc_scratch; looked up on the first call per device.
+int noalloc_scratch(DeviceInfo* d, void** out) {
+  std::lock_guard<std::mutex> lk(g_dev_mu);
+  if (d->noalloc_scratch == nullptr) {
+    void* p = nullptr;
+    if (int rc = cuda_check(cudaGetSymbolAddress(&p, g_noalloc_scratch), "cudaGetSymbolAddress(scratch)"))
+      return rc;
+    d->noalloc_scratch = p;
+  }
+  *out = d->noalloc_scratch;
   return MOE_OK;
 }
 
@@ -247,6 +268,30 @@ int moe_forward(const void* hidden, const float* hidden_scale, const void* w13_p
   return forward_impl(hidden, hidden_scale, w13_packed, w13_scale, w2_packed, w2_scale, logits, bias,
                       routed_scaling_factor, local_expert_offset, T, E_local, out_bf16, workspace,
                       workspace_bytes, stream, nullptr);
+}
+
+int moe_forward_noalloc(const void* hidden, const float* hidden_scale, const void* w13_packed,
+                        const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                        const float* logits, const float* bias, float routed_scaling_factor,
+                        int local_expert_offset, int T, int E_local, void* out_bf16, void* stream) {
+  if (T < 0) return fail(MOE_ERR_INVALID, "hidden must be [T, 7168]");
+  if (E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "W13_packed must be [E_local, ...] with 1 <= E_local <= 256");
+  if (T == 0) return MOE_OK;
+  const size_t need = make_workspace(T, E_local).total;
+  if (need > NOALLOC_SCRATCH_BYTES)
+    return fail(MOE_ERR_WORKSPACE,
+                "moe_forward_noalloc: T=" + std::to_string(T) + " with E_local=" + std::to_string(E_local) +
+                    " needs " + std::to_string(need) + " bytes of scratch, more than the " +
+                    std::to_string(NOALLOC_SCRATCH_BYTES) +
+                    " bytes of the library's static scratch (enough for T <= 64 with 32 local "
+                    "experts); call moe_forward with a workspace instead");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  void* scratch = nullptr;
+  if (int rc = noalloc_scratch(d, &scratch)) return rc;
+  return forward_impl(hidden, hidden_scale, w13_packed, w13_scale, w2_packed, w2_scale, logits, bias,
+                      routed_scaling_factor, local_expert_offset, T, E_local, out_bf16, scratch,
+                      NOALLOC_SCRATCH_BYTES, stream, nullptr);
 }
 
 int moe_forward_profiled(const void* hidden, const float* hidden_scale, const void* w13_packed,

@@ -79,6 +79,31 @@ int moe_forward(const void* hidden, const float* hidden_scale, const void* w13_p
                 int local_expert_offset, int T, int E_local, void* out_bf16, void* workspace,
                 size_t workspace_bytes, void* stream);
 
+/* Size of the static device scratch used by moe_forward_noalloc: 72 MiB per device. */
+#define MOE_NOALLOC_SCRATCH_BYTES (72u << 20)
+
+/* moe_forward for callers that cannot allocate device memory - for example a plugin whose host
+ * application owns all GPU memory through its own pool, or a code path where a cudaMalloc
+ * (which may synchronise the device and fail under memory pressure) is not allowed. It takes
+ * no workspace: its scratch is a static array inside this library, MOE_NOALLOC_SCRATCH_BYTES
+ * bytes on every device that loads the library, held until the process exits. The caller still
+ * passes all inputs and the output, exactly as for moe_forward.
+ *   - Limit: moe_forward_workspace_bytes(T, E_local) must not exceed MOE_NOALLOC_SCRATCH_BYTES
+ *     (e.g. T <= 64 tokens with 32 local experts); larger calls return MOE_ERR_WORKSPACE and
+ *     do nothing.
+ *   - The first call on a device looks up the scratch address (and does the same one-time
+ *     kernel set-up as moe_forward); make that first call before any stream capture.
+ *   - Every call on a device uses the same scratch, so calls that can overlap on the GPU (on
+ *     different streams, or from different threads) race and must be serialised by the
+ *     caller. The scratch keeps the previous call's contents; each call resets what it needs.
+ *   - It calls no cudaMalloc, cudaFree or other allocating routine.
+ * No counterpart in the reference (its moe_forward allocates through PyTorch,
+ * kernels/moe.cu:819-833). */
+int moe_forward_noalloc(const void* hidden, const float* hidden_scale, const void* w13_packed,
+                        const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                        const float* logits, const float* bias, float routed_scaling_factor,
+                        int local_expert_offset, int T, int E_local, void* out_bf16, void* stream);
+
 /* moe_forward that also records events[0..6] (cudaEvent_t) on `stream`: before the first
  * launch and after each of its six kernels (route, dispatch, gather, gemm1, gemm2,
  * combine), for per-kernel timing. No reference counterpart (instrumentation only). */

@@ -1,0 +1,73 @@
+"""moe_forward_noalloc: the MoE forward for callers that cannot allocate device memory.
+
+Some hosts of this library (a plugin inside a server that owns every GPU byte through its own
+pool, or a code path where cudaMalloc is not allowed) cannot provide the workspace that
+moe_forward needs. moe_forward_noalloc runs the same kernels on a static scratch array inside
+the library instead. This file checks, through the C ABI, that it returns what moe_forward
+returns on two calls in a row (different inputs, so stale scratch contents would show), and that
+a call larger than its scratch is refused. It is named to be collected last and also passes
+when run alone in a fresh process (its first call does the per-device set-up).
+"""
+import importlib
+
+import numpy as np
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+ATOL, RTOL = 1e-2, 2e-2
+
+
+def _args(pkg, inp):
+    w13p = pkg.pack_w13(inp["gemm1_weights"])
+    w2p = pkg.pack_w2(inp["gemm2_weights"])
+    keep = dict(
+        hidden=inp["hidden_states"], hs=inp["hidden_states_scale"].float().contiguous(), w13p=w13p,
+        s13=inp["gemm1_weights_scale"].float().contiguous(), w2p=w2p,
+        s2=inp["gemm2_weights_scale"].float().contiguous(),
+        lg=inp["routing_logits"].float().contiguous(),
+        b=inp["routing_bias"].float().reshape(-1).contiguous())
+    return keep
+
+
+def _with_workspace(pkg, k, inp):
+    return pkg.moe_forward(k["hidden"], k["hs"], k["w13p"], k["s13"], k["w2p"], k["s2"], k["lg"], k["b"],
+                           inp["routed_scaling_factor"], inp["local_expert_offset"])
+
+
+def _noalloc(lib, k, inp, out):
+    T, E = k["hidden"].shape[0], k["w13p"].shape[0]
+    return lib.moe_forward_noalloc(
+        k["hidden"].data_ptr(), k["hs"].data_ptr(), k["w13p"].data_ptr(), k["s13"].data_ptr(),
+        k["w2p"].data_ptr(), k["s2"].data_ptr(), k["lg"].data_ptr(), k["b"].data_ptr(),
+        float(inp["routed_scaling_factor"]), int(inp["local_expert_offset"]), T, E, out.data_ptr(),
+        torch.cuda.current_stream().cuda_stream)
+
+
+def test_noalloc_matches_moe_forward_twice(pkg, oracle):
+    native = importlib.import_module("15642_moe_b200._native")
+    lib = native.cuda_lib()
+    cases = [pkg.CONFIGS[1], pkg.MoEConfig(T=16, seed=11, local_expert_offset=64)]
+    for cfg in cases:                       # two calls in a row, different routing
+        inp = pkg.make_inputs(cfg, "cuda")
+        k = _args(pkg, inp)
+        ref = _with_workspace(pkg, k, inp)
+        out = torch.full_like(ref, float("nan"))
+        native.check(_noalloc(lib, k, inp, out))
+        torch.cuda.synchronize()
+        a = ref.view(torch.int16).cpu().numpy().view(np.uint16)
+        b = out.view(torch.int16).cpu().numpy().view(np.uint16)
+        r = oracle.check_tolerance(a, b, ATOL, RTOL)
+        assert r["bad"] == 0, (cfg, r)
+        assert np.isfinite(oracle.bf16_bits_to_f32(b)).all()
+    assert pkg.device_status(reset=True) == 0
+
+
+def test_noalloc_refuses_calls_beyond_its_scratch(pkg):
+    native = importlib.import_module("15642_moe_b200._native")
+    lib = native.cuda_lib()
+    assert lib.moe_forward_workspace_bytes(64, 32) <= (72 << 20) < lib.moe_forward_workspace_bytes(4096, 32)
+    null = None
+    rc = lib.moe_forward_noalloc(null, null, null, null, null, null, null, null, 1.0, 0, 4096, 32, null, null)
+    assert rc == 3
+    assert b"static scratch" in lib.moe_last_error()
