@@ -6,13 +6,15 @@
  * (128j..128j+127) and the matching 128 X2 rows (2048+128j..) of the expert's W13, so the
  * SwiGLU of one 128-wide intermediate block is computed inside one CTA.
  *
- * One persistent CTA per SM, warp-specialised:
+ * One persistent CTA per SM, warp-specialised (three warpgroups, 384 threads):
  *   warp 0      producer: cp.async.bulk of pre-swizzled 16 KB A tiles and 32 KB W13 tiles
  *               into a 4-stage shared-memory ring (mbarrier complete_tx)
- *   warp 1      MMA: 4 x tcgen05.mma kind::f8f6f4 (M=128, N=256, K=32) per 128-K block into
- *               one of two TMEM accumulators (2 x 256 columns)
- *   warps 4-11  epilogue: after each 128-K block, read the raw partial from TMEM and promote it
- *               with the block scales, acc += raw * a_scale[row, kb] * w_scale[nblk, kb]
+ *   warp 1      MMA: per 128-K block, 4 x tcgen05.mma kind::f8f6f4 (M=128, K=32) over the
+ *               256 columns, as ACC_SPLIT groups of N = 256 / ACC_SPLIT, each group into its
+ *               own TMEM accumulator; all 512 TMEM columns rotate as accumulators so K blocks
+ *               stay in flight while the epilogue promotes earlier ones.
+ *   warps 4-11  epilogue: for every accumulator, read the raw 128-K partial from TMEM and
+ *               promote it with the block scales, acc += raw * a_scale[row, kb] * w_scale[nb, kb]
  *               (the reference's fp32 dequantisation, moe_ref.py:59-79, applied per block);
  *               at the end apply SwiGLU and write C as two e4m3 terms (hi + lo) with one fp32
  *               scale per (row, 128-column block), laid out as SW128 tiles for GEMM2.
@@ -45,12 +47,22 @@ constexpr int G1_STAGE_BYTES = G1_A_BYTES + G1_B_BYTES;
 constexpr int G1_THREADS = GEMM_THREADS;
 constexpr int G1_CTRL_BYTES = 4096;
 constexpr int G1_SMEM = G1_STAGES * G1_STAGE_BYTES + G1_CTRL_BYTES + 1024;
+// TMEM accumulators: a 256-column unit is computed per 128-K block as ACC_SPLIT MMA groups of
+// N = ACC_COLS, each into its own accumulator; all 512 TMEM columns rotate as ACC_BUFS
+// accumulators, so ACC_BUFS / ACC_SPLIT K blocks can be in flight at once.
+#ifndef MOE_ACC_SPLIT
+#define MOE_ACC_SPLIT 1
+#endif
+constexpr int ACC_SPLIT = MOE_ACC_SPLIT;
+constexpr int ACC_COLS = 256 / ACC_SPLIT;
+constexpr int ACC_BUFS = 512 / ACC_COLS;
+static_assert(ACC_SPLIT == 1 || ACC_SPLIT == 2, "unit is split into one or two accumulators");
 
 struct G1Ctrl {
   uint64_t full[G1_STAGES];
   uint64_t empty[G1_STAGES];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t tfull[ACC_BUFS];
+  uint64_t tempty[ACC_BUFS];
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
@@ -82,6 +94,56 @@ __device__ __forceinline__ void quant_hi_lo16(const float* x, uint4& hi, uint4& 
   lo = make_uint4(l[0], l[1], l[2], l[3]);
 }
 
+// Load 64 consecutive fp32 columns of this thread's TMEM lane and wait for completion.
+__device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
+  float a[32], b[32];
+  tmem_ld32(taddr, a);
+  tmem_ld32(taddr + 32u, b);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    v[i] = a[i];
+    v[32 + i] = b[i];
+  }
+}
+
+// Epilogue step of one 128-K block of a 256-column unit, for this thread's row (TMEM lane
+// quadrant `t_lane`): columns [64*hf, 64*hf + 64) of the unit's first 128-column half are
+// promoted into acc0 with factor f0, the same columns of the second half into acc1 with f1.
+// An accumulator is released as soon as its values are in registers, before the FMAs, so the
+// tensor core can refill it while the promotion runs.
+template <class Ctrl>
+__device__ __forceinline__ bool promote_block(Ctrl* ctl, uint32_t tmem, uint32_t t_lane, int hf,
+                                              uint32_t it, float f0, float* acc0, float f1,
+                                              float* acc1, volatile int* abort_flag) {
+  float v[64];
+#pragma unroll
+  for (int half = 0; half < 2; ++half) {
+    const uint32_t hidx = ACC_SPLIT == 2 ? 2 * it + half : it;
+    const uint32_t q = hidx % ACC_BUFS, use = hidx / ACC_BUFS;
+    if (ACC_SPLIT == 2 || half == 0) {
+      if (!mbar_wait_warp(&ctl->tfull[q], use & 1u, abort_flag, ST_TIMEOUT_EPILOGUE)) return false;
+      tc_fence_after();
+    }
+    const uint32_t col = q * ACC_COLS + (ACC_SPLIT == 1 ? half * 128u : 0u) + hf * 64u;
+    tmem_ld64(tmem + t_lane + col, v);
+    if (ACC_SPLIT == 2 || half == 1) {
+      tc_fence_before();
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(&ctl->tempty[q]);
+    }
+    float* acc = half == 0 ? acc0 : acc1;
+    const float f = half == 0 ? f0 : f1;
+    float w[32];
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = v[i];
+    fma32_scaled(acc, w, f);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) w[i] = v[32 + i];
+    fma32_scaled(acc + 32, w, f);
+  }
+  return true;
+}
+
 __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(Gemm1Args p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_1024(smem_raw);
@@ -97,7 +159,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(Gemm1Args p
       mbar_init(&ctl->empty[s], 1);
     }
 #pragma unroll
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < ACC_BUFS; ++b) {
       mbar_init(&ctl->tfull[b], 1);
       mbar_init(&ctl->tempty[b], 8);
     }
@@ -106,7 +168,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(Gemm1Args p
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_alloc(&ctl->tmem_base, ACC_BUFS * ACC_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -159,25 +221,36 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(Gemm1Args p
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
+      constexpr uint32_t idesc = idesc_e4m3_f32(128, ACC_COLS);
       uint32_t it = 0;
-      for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
-        for (int kb = 0; kb < HB; ++kb, ++it) {
+      bool stop = false;
+      for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x) {
+        for (int kb = 0; kb < HB && !stop; ++kb, ++it) {
           const int s = it % G1_STAGES;
           const uint32_t ph = (it / G1_STAGES) & 1u;
-          const uint32_t b = it & 1u, use = it >> 1;
-          if (!mbar_wait(&ctl->tempty[b], (use & 1u) ^ 1u, abort_flag, ST_TIMEOUT_MMA)) break;
-          if (!mbar_wait(&ctl->full[s], ph, abort_flag, ST_TIMEOUT_MMA)) break;
-          tc_fence_after();
+          if (!mbar_wait(&ctl->full[s], ph, abort_flag, ST_TIMEOUT_MMA)) {
+            stop = true;
+            break;
+          }
           const uint32_t a_addr = smem_u32(smem + s * G1_STAGE_BYTES);
-          const uint32_t b_addr = a_addr + G1_A_BYTES;
-          const uint32_t d = tmem + b * 256u;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk)
-            tc_mma_f8(d, sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32), idesc,
-                      kk > 0 ? 1u : 0u);
-          tc_commit(&ctl->empty[s]);
-          tc_commit(&ctl->tfull[b]);
+          for (int h = 0; h < ACC_SPLIT; ++h) {   // ACC_SPLIT = 2: h = 0 X1 rows, h = 1 X2 rows
+            const uint32_t hidx = ACC_SPLIT * it + h;
+            const uint32_t q = hidx % ACC_BUFS, use = hidx / ACC_BUFS;
+            if (!mbar_wait(&ctl->tempty[q], (use & 1u) ^ 1u, abort_flag, ST_TIMEOUT_MMA)) {
+              stop = true;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t b_addr = a_addr + G1_A_BYTES + h * ACC_COLS * 128;
+            const uint32_t d = tmem + q * ACC_COLS;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk)
+              tc_mma_f8(d, sdesc_k_sw128(a_addr + kk * 32), sdesc_k_sw128(b_addr + kk * 32), idesc,
+                        kk > 0 ? 1u : 0u);
+            tc_commit(&ctl->tfull[q]);
+          }
+          if (!stop) tc_commit(&ctl->empty[s]);
         }
       }
       if (*abort_flag) {
@@ -189,10 +262,10 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(Gemm1Args p
   } else if (warp >= 4) {
     // ---------------- epilogue (warps 4..11) ----------------
     regs_inc<REGS_EPI>();
-    const int q = warp & 3;            // TMEM lane quadrant this warp may access
-    const int hf = (warp - 4) >> 2;    // column half: 64 X1 + 64 X2 columns
-    const int row = q * 32 + lane;
-    const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+    const int q4 = warp & 3;            // TMEM lane quadrant this warp may access
+    const int hf = (warp - 4) >> 2;     // column half: 64 X1 + 64 X2 columns
+    const int row = q4 * 32 + lane;
+    const uint32_t t_lane = static_cast<uint32_t>(q4 * 32) << 16;
     uint32_t it = 0, unit_no = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++unit_no) {
       const int tile = u / G1_NT, j = u % G1_NT;
@@ -206,47 +279,34 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(Gemm1Args p
         accg[i] = 0.0f;
         accu[i] = 0.0f;
       }
-      float sa_next = __ldg(sa_ptr);
+      // Scale factors of the next K block are loaded one block ahead, off the critical path.
+      float na = __ldg(sa_ptr), ng = __ldg(sg_ptr), nu = __ldg(su_ptr);
       bool aborted = false;
       for (int kb = 0; kb < HB; ++kb, ++it) {
-        const float sa = sa_next;
-        if (kb + 1 < HB) sa_next = __ldg(sa_ptr + (kb + 1) * TILE_M);
-        const float fg = sa * __ldg(sg_ptr + kb);
-        const float fu = sa * __ldg(su_ptr + kb);
-        const uint32_t b = it & 1u, use = it >> 1;
-        if (!mbar_wait_warp(&ctl->tfull[b], use & 1u, abort_flag, ST_TIMEOUT_EPILOGUE)) {
+        const float fg = na * ng, fu = na * nu;
+        if (kb + 1 < HB) {
+          na = __ldg(sa_ptr + (kb + 1) * TILE_M);
+          ng = __ldg(sg_ptr + kb + 1);
+          nu = __ldg(su_ptr + kb + 1);
+        }
+        if (!promote_block(ctl, tmem, t_lane, hf, it, fg, accg, fu, accu, abort_flag)) {
           aborted = true;
           break;
         }
-        tc_fence_after();
-        const uint32_t base = tmem + t_lane + b * 256u + hf * 64u;
-        float v[32];
-        tmem_ld32(base, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) accg[i] = fmaf(v[i], fg, accg[i]);
-        tmem_ld32(base + 32u, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) accg[32 + i] = fmaf(v[i], fg, accg[32 + i]);
-        tmem_ld32(base + 128u, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) accu[i] = fmaf(v[i], fu, accu[i]);
-        tmem_ld32(base + 160u, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) accu[32 + i] = fmaf(v[i], fu, accu[32 + i]);
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->tempty[b]);
       }
       // Every epilogue thread passes this barrier once per unit; the OR makes the decision
       // to stop uniform, so no thread is left waiting on a barrier the others skipped.
       if (named_bar_or(1, 256, aborted)) break;
 
-      // SwiGLU: C = X1 * SiLU(X2)  (moe_ref.py:129-130)
+      // SwiGLU: C = X1 * SiLU(X2)  (moe_ref.py:129-130). C is re-encoded to ~2^-8 relative
+      // precision below, so the fast exponential and division (a few ulp) are exact enough;
+      // the IEEE-rounded versions made this once-per-unit step cost as much as the K loop.
+      // For X2 -> -inf, __expf -> inf and __fdividef returns 0, the limit of SiLU.
       float amax = 0.0f;
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
         const float x2 = accu[i];
-        const float c = (x2 / (1.0f + expf(-x2))) * accg[i];
+        const float c = __fdividef(x2, 1.0f + __expf(-x2)) * accg[i];
         accg[i] = c;
         amax = fmaxf(amax, fabsf(c));
       }
@@ -254,8 +314,9 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(Gemm1Args p
       named_bar_or(2, 256, false);
       amax = fmaxf(amax, ctl->amax[unit_no & 1][hf ^ 1][row]);
       const float scale = amax > 0.0f ? amax / 448.0f : 1.0f;
+      const float inv = amax > 0.0f ? 448.0f / amax : 1.0f;
 #pragma unroll
-      for (int i = 0; i < 64; ++i) accg[i] = __fdiv_rn(accg[i], scale);
+      for (int i = 0; i < 64; ++i) accg[i] *= inv;
 
       const size_t blk = (static_cast<size_t>(tile) * IB + j) * TILE_BYTES + row * 128;
 #pragma unroll
@@ -275,7 +336,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(Gemm1Args p
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, 512);
+  if (warp == 1) tmem_dealloc(tmem, ACC_BUFS * ACC_COLS);
 }
 
 }  // namespace moe

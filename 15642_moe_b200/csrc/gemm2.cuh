@@ -4,16 +4,21 @@
  *
  * C arrives from GEMM1 as two e4m3 terms sharing one fp32 scale per (row, 128-block):
  * C ~= scale * (hi + lo). Both terms are multiplied against the same W2 tile and accumulate
- * into the same TMEM accumulator (8 x tcgen05.mma per 128-K block), so the intermediate
- * keeps ~2^-8 relative precision instead of e4m3's 2^-4 while W2 stays FP8 in HBM.
+ * into the same TMEM accumulator, so the intermediate keeps ~2^-8 relative precision instead
+ * of e4m3's 2^-4 while W2 stays FP8 in HBM.
  *
- * Work unit = (128-row tile, 256-column tile of H). Same warp roles as GEMM1:
- *   warp 0 producer (bulk copies: 16 KB hi + 16 KB lo + 32 KB W2 per stage, 3 stages),
- *   warp 1 MMA issuer, warps 4-11 epilogue (per-128-K promotion with c_scale * w2_scale,
- *   final multiply by the route weight, fp32 rows written to the partial buffer).
+ * Work unit = (128-row tile, 256 hidden rows of W2 = two 128-wide output halves). Same warp
+ * roles and rotating TMEM accumulators as GEMM1:
+ *   warp 0      producer (bulk copies: 16 KB hi + 16 KB lo + 32 KB W2 per stage, 3 stages)
+ *   warp 1      MMA: per 128-K block, hi then lo for each of the 4 K steps (M=128, K=32), in
+ *               ACC_SPLIT groups of N = 256 / ACC_SPLIT columns, each into its own accumulator
+ *   warps 4-11  epilogue: per accumulator, promote with c_scale[row, kb] * w2_scale[hb, kb];
+ *               at the end multiply by the route weight and write the fp32 rows to `partial`
+ *               (dense: one row per local route).
  */
 #pragma once
 #include "moe_common.cuh"
+#include "gemm1.cuh"
 
 namespace moe {
 
@@ -44,8 +49,8 @@ constexpr int G2_SMEM = G2_STAGES * G2_STAGE_BYTES + G2_CTRL_BYTES + 1024;
 struct G2Ctrl {
   uint64_t full[G2_STAGES];
   uint64_t empty[G2_STAGES];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
+  uint64_t tfull[ACC_BUFS];
+  uint64_t tempty[ACC_BUFS];
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
@@ -67,7 +72,7 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(Gemm2Args
       mbar_init(&ctl->empty[s], 1);
     }
 #pragma unroll
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < ACC_BUFS; ++b) {
       mbar_init(&ctl->tfull[b], 1);
       mbar_init(&ctl->tempty[b], 8);
     }
@@ -76,7 +81,7 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(Gemm2Args
     fence_mbar_init();
   }
   if (warp == 1) {
-    tmem_alloc(&ctl->tmem_base, 512);
+    tmem_alloc(&ctl->tmem_base, ACC_BUFS * ACC_COLS);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -130,28 +135,39 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(Gemm2Args
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(128, 256);
+      constexpr uint32_t idesc = idesc_e4m3_f32(128, ACC_COLS);
       uint32_t it = 0;
-      for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
-        for (int ib = 0; ib < IB; ++ib, ++it) {
+      bool stop = false;
+      for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x) {
+        for (int ib = 0; ib < IB && !stop; ++ib, ++it) {
           const int s = it % G2_STAGES;
           const uint32_t ph = (it / G2_STAGES) & 1u;
-          const uint32_t b = it & 1u, use = it >> 1;
-          if (!mbar_wait(&ctl->tempty[b], (use & 1u) ^ 1u, abort_flag, ST_TIMEOUT_MMA)) break;
-          if (!mbar_wait(&ctl->full[s], ph, abort_flag, ST_TIMEOUT_MMA)) break;
-          tc_fence_after();
+          if (!mbar_wait(&ctl->full[s], ph, abort_flag, ST_TIMEOUT_MMA)) {
+            stop = true;
+            break;
+          }
           const uint32_t hi_addr = smem_u32(smem + s * G2_STAGE_BYTES);
           const uint32_t lo_addr = hi_addr + G2_A_BYTES;
-          const uint32_t b_addr = hi_addr + 2 * G2_A_BYTES;
-          const uint32_t d = tmem + b * 256u;
 #pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t bd = sdesc_k_sw128(b_addr + kk * 32);
-            tc_mma_f8(d, sdesc_k_sw128(hi_addr + kk * 32), bd, idesc, kk > 0 ? 1u : 0u);
-            tc_mma_f8(d, sdesc_k_sw128(lo_addr + kk * 32), bd, idesc, 1u);
+          for (int h = 0; h < ACC_SPLIT; ++h) {   // output columns [ACC_COLS h, ACC_COLS (h+1))
+            const uint32_t hidx = ACC_SPLIT * it + h;
+            const uint32_t q = hidx % ACC_BUFS, use = hidx / ACC_BUFS;
+            if (!mbar_wait(&ctl->tempty[q], (use & 1u) ^ 1u, abort_flag, ST_TIMEOUT_MMA)) {
+              stop = true;
+              break;
+            }
+            tc_fence_after();
+            const uint32_t b_addr = hi_addr + 2 * G2_A_BYTES + h * ACC_COLS * 128;
+            const uint32_t d = tmem + q * ACC_COLS;
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              const uint64_t bd = sdesc_k_sw128(b_addr + kk * 32);
+              tc_mma_f8(d, sdesc_k_sw128(hi_addr + kk * 32), bd, idesc, kk > 0 ? 1u : 0u);
+              tc_mma_f8(d, sdesc_k_sw128(lo_addr + kk * 32), bd, idesc, 1u);
+            }
+            tc_commit(&ctl->tfull[q]);
           }
-          tc_commit(&ctl->empty[s]);
-          tc_commit(&ctl->tfull[b]);
+          if (!stop) tc_commit(&ctl->empty[s]);
         }
       }
       if (*abort_flag) {
@@ -162,55 +178,47 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(Gemm2Args
   } else if (warp >= 4) {
     // ---------------- epilogue (warps 4..11) ----------------
     regs_inc<REGS_EPI>();
-    const int q = warp & 3;
-    const int hf = (warp - 4) >> 2;    // which 128 of the 256 output columns
-    const int row = q * 32 + lane;
-    const uint32_t t_lane = static_cast<uint32_t>(q * 32) << 16;
+    const int q4 = warp & 3;
+    const int hf = (warp - 4) >> 2;    // which 64 columns of each 128-wide half
+    const int row = q4 * 32 + lane;
+    const uint32_t t_lane = static_cast<uint32_t>(q4 * 32) << 16;
     uint32_t it = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int tile = u / G2_NT, nt = u % G2_NT;
       const int e = checked_expert(p.tile_expert[tile], p.E_local);
-      const int hb = nt * 2 + hf;
       const float* cs_ptr = p.c_scale + static_cast<size_t>(tile) * IB * TILE_M + row;
-      const float* ws_ptr = p.w2_scale + (static_cast<size_t>(e) * HB + hb) * IB;
+      const float* ws0 = p.w2_scale + (static_cast<size_t>(e) * HB + 2 * nt) * IB;
+      const float* ws1 = ws0 + IB;
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
-      float cs_next = __ldg(cs_ptr);
+      float nc = __ldg(cs_ptr), n0 = __ldg(ws0), n1 = __ldg(ws1);
       bool aborted = false;
       for (int ib = 0; ib < IB; ++ib, ++it) {
-        const float cs = cs_next;
-        if (ib + 1 < IB) cs_next = __ldg(cs_ptr + (ib + 1) * TILE_M);
-        const float f = cs * __ldg(ws_ptr + ib);
-        const uint32_t b = it & 1u, use = it >> 1;
-        if (!mbar_wait_warp(&ctl->tfull[b], use & 1u, abort_flag, ST_TIMEOUT_EPILOGUE)) {
+        const float f0 = nc * n0, f1 = nc * n1;
+        if (ib + 1 < IB) {
+          nc = __ldg(cs_ptr + (ib + 1) * TILE_M);
+          n0 = __ldg(ws0 + ib + 1);
+          n1 = __ldg(ws1 + ib + 1);
+        }
+        if (!promote_block(ctl, tmem, t_lane, hf, it, f0, acc, f1, acc + 64, abort_flag)) {
           aborted = true;
           break;
         }
-        tc_fence_after();
-        const uint32_t base = tmem + t_lane + b * 256u + hf * 128u;
-        float v[32];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          tmem_ld32(base + c * 32u, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) acc[c * 32 + i] = fmaf(v[i], f, acc[c * 32 + i]);
-        }
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&ctl->tempty[b]);
       }
       if (named_bar_or(1, 256, aborted)) break;
 
       if (row < p.tile_rows[tile]) {
         const float w = p.route_w[static_cast<size_t>(tile) * TILE_M + row];
-        float4* dst = reinterpret_cast<float4*>(p.partial +
-                                                static_cast<size_t>(p.tile_dense[tile] + row) * H +
-                                                nt * 256 + hf * 128);
+        float* base = p.partial + static_cast<size_t>(p.tile_dense[tile] + row) * H + nt * 256 + hf * 64;
 #pragma unroll
-        for (int i = 0; i < 32; ++i)
-          dst[i] = make_float4(acc[4 * i] * w, acc[4 * i + 1] * w, acc[4 * i + 2] * w,
-                               acc[4 * i + 3] * w);
+        for (int h = 0; h < 2; ++h) {
+          float4* dst = reinterpret_cast<float4*>(base + h * 128);
+#pragma unroll
+          for (int i = 0; i < 16; ++i)
+            dst[i] = make_float4(acc[h * 64 + 4 * i] * w, acc[h * 64 + 4 * i + 1] * w,
+                                 acc[h * 64 + 4 * i + 2] * w, acc[h * 64 + 4 * i + 3] * w);
+        }
       }
     }
   }
@@ -219,7 +227,7 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(Gemm2Args
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 1) tmem_dealloc(tmem, 512);
+  if (warp == 1) tmem_dealloc(tmem, ACC_BUFS * ACC_COLS);
 }
 
 }  // namespace moe

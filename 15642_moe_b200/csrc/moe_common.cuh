@@ -98,14 +98,18 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
 
+// Test for completion of the phase with the given parity. When it is not complete the thread
+// is suspended in hardware (no issue slots used) until it completes or about SUSPEND_NS pass,
+// so waiting warps do not slow down the warps that share their SM sub-partition.
+constexpr uint32_t SUSPEND_NS = 1000000;  // 1 ms per try; the caller bounds the total wait
 __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "n"(SUSPEND_NS)
       : "memory");
   return ok != 0;
 }
@@ -118,9 +122,7 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = globaltimer();
   while (true) {
-#pragma unroll 1
-    for (int i = 0; i < 32; ++i)
-      if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (globaltimer() - t0 > WAIT_LIMIT_NS) {
       *abort_flag = 1;
@@ -243,6 +245,20 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// acc[i] += v[i] * f for 32 values, as 16 packed fp32x2 FMAs (each lane IEEE fmaf).
+__device__ __forceinline__ void fma32_scaled(float* acc, const float (&v)[32], float f) {
+  uint64_t ff;
+  asm("mov.b64 %0, {%1, %1};" : "=l"(ff) : "f"(f));
+#pragma unroll
+  for (int i = 0; i < 32; i += 2) {
+    uint64_t a, b;
+    asm("mov.b64 %0, {%1, %2};" : "=l"(a) : "f"(acc[i]), "f"(acc[i + 1]));
+    asm("mov.b64 %0, {%1, %2};" : "=l"(b) : "f"(v[i]), "f"(v[i + 1]));
+    asm("fma.rn.f32x2 %0, %1, %2, %0;" : "+l"(a) : "l"(b), "l"(ff));
+    asm("mov.b64 {%0, %1}, %2;" : "=f"(acc[i]), "=f"(acc[i + 1]) : "l"(a));
+  }
+}
+
 // Shared-memory matrix descriptor: K-major operand, 128-byte swizzle, 8-row atoms of
 // 1024 bytes (SBO), version 1 (sm_100). `saddr` is the shared-window byte address of the
 // first row of the tile plus the K offset (multiples of 32 bytes inside the atom).
@@ -280,12 +296,12 @@ __device__ __forceinline__ void regs_inc() {
 }
 
 // GEMM CTA shape shared by both tcgen05 kernels: warpgroup 0 = producer warp, MMA warp and
-// two idle warps (40 registers each); warpgroups 1-2 = eight epilogue warps (232 registers).
-// 128 * 40 + 256 * 232 = 64512 = 384 * 168, the launch allocation at 168 registers/thread;
+// two idle warps (56 registers each); warpgroups 1-2 = eight epilogue warps (224 registers).
+// 128 * 56 + 256 * 224 = 64512 = 384 * 168, the launch allocation at 168 registers/thread;
 // the host refuses to launch if ptxas gave the kernel fewer (setmaxnreg.inc would stall).
 constexpr int GEMM_THREADS = 384;
-constexpr int REGS_CTRL = 40;
-constexpr int REGS_EPI = 232;
+constexpr int REGS_CTRL = 56;
+constexpr int REGS_EPI = 224;
 constexpr int GEMM_LAUNCH_REGS_MIN = (128 * REGS_CTRL + 256 * REGS_EPI + GEMM_THREADS - 1) / GEMM_THREADS;
 
 // Named barrier among `nthreads` threads (ids 1..15; id 0 is __syncthreads) that also
