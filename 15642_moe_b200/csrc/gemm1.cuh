@@ -7,8 +7,8 @@
  * SwiGLU of one 128-wide intermediate block is computed inside one CTA.
  *
  * One persistent CTA per SM, warp-specialised (three warpgroups, 384 threads):
- *   warp 0      producer: cp.async.bulk of pre-swizzled 16 KB A tiles and 32 KB W13 tiles
- *               into a 4-stage shared-memory ring (mbarrier complete_tx)
+ *   warp 0      producer: cp.async.bulk of the 16 KB A tile image (routed rows, written by the
+ *               gather kernel) and the pre-swizzled 32 KB W13 tile into a 4-stage ring
  *   warp 1      MMA: per 128-K block, 4 x tcgen05.mma kind::f8f6f4 (M=128, K=32) over the
  *               256 columns, as ACC_SPLIT groups of N = 256 / ACC_SPLIT, each group into its
  *               own TMEM accumulator; all 512 TMEM columns rotate as accumulators so K blocks
@@ -27,14 +27,14 @@
 namespace moe {
 
 struct Gemm1Args {
-  const uint8_t* a_tiled;   // [tiles, 56, 128, 128] SW128
+  const uint8_t* a_tiled;   // [tiles, 56, 128, 128] SW128 images of the routed hidden rows
   const float* a_scale;     // [tiles, 56, 128]
   const uint8_t* w13p;      // [E, 16, 56, 256, 128] SW128 (packed by pack_w13_kernel)
   const float* w13_scale;   // [E, 32, 56]
-  const int* tile_expert;   // [tiles]
-  const int* n_tiles;       // [1]
-  int tiles_max;            // capacity of the workspace tile arrays
-  int E_local;              // number of local experts (bounds of tile_expert)
+  const int* counts;        // [E_local] routes per local expert
+  int slots;                // bound on a count (T)
+  int tiles_max;            // capacity of the tile arrays
+  int E_local;
   uint8_t* c_hi;            // [tiles, 16, 128, 128] SW128
   uint8_t* c_lo;            // [tiles, 16, 128, 128] SW128
   float* c_scale;           // [tiles, 16, 128]
@@ -45,7 +45,7 @@ constexpr int G1_A_BYTES = TILE_BYTES;
 constexpr int G1_B_BYTES = 2 * TILE_BYTES;
 constexpr int G1_STAGE_BYTES = G1_A_BYTES + G1_B_BYTES;
 constexpr int G1_THREADS = GEMM_THREADS;
-constexpr int G1_CTRL_BYTES = 4096;
+constexpr int G1_CTRL_BYTES = 8192;
 constexpr int G1_SMEM = G1_STAGES * G1_STAGE_BYTES + G1_CTRL_BYTES + 1024;
 // TMEM accumulators: a 256-column unit is computed per 128-K block as ACC_SPLIT MMA groups of
 // N = ACC_COLS, each into its own accumulator; all 512 TMEM columns rotate as ACC_BUFS
@@ -67,6 +67,7 @@ struct G1Ctrl {
   uint32_t tmem_base;
   int abort_flag;
   float amax[2][2][TILE_M];  // [unit parity][column half][row]
+  TileMap map;
 };
 static_assert(sizeof(G1Ctrl) <= G1_CTRL_BYTES, "control block too large");
 
@@ -144,12 +145,28 @@ __device__ __forceinline__ bool promote_block(Ctrl* ctl, uint32_t tmem, uint32_t
   return true;
 }
 
-__global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(Gemm1Args p) {
+// Expert, tile-in-expert and valid rows of global tile `tile`.
+struct TileInfo {
+  int e, m, rows;
+};
+__device__ __forceinline__ TileInfo locate(const TileMap* tm, const int* counts, int E_local,
+                                           int tile, int cap) {
+  TileInfo ti;
+  ti.e = tile_expert(tm, E_local, tile);
+  ti.m = tile - tm->tile_off[ti.e];
+  const int c = min(max(counts[ti.e], 0), cap);
+  ti.rows = min(TILE_M, c - ti.m * TILE_M);
+  return ti;
+}
+
+__global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __grid_constant__ Gemm1Args p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_1024(smem_raw);
   G1Ctrl* ctl = reinterpret_cast<G1Ctrl*>(smem + G1_STAGES * G1_STAGE_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_units = clamp_tiles(*p.n_tiles, p.tiles_max) * G1_NT;
+  if (warp == 0) build_tile_map(&ctl->map, p.counts, p.E_local, p.slots);
+  __syncthreads();
+  const int n_units = clamp_tiles(ctl->map.tile_off[p.E_local], p.tiles_max) * G1_NT;
   if (static_cast<int>(blockIdx.x) >= n_units) return;  // uniform per CTA, before any TMEM use
 
   if (threadIdx.x == 0) {
@@ -187,7 +204,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(Gemm1Args p
       uint32_t it = 0;
       for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
         const int tile = u / G1_NT, j = u % G1_NT;
-        const int e = checked_expert(p.tile_expert[tile], p.E_local);
+        const int e = tile_expert(&ctl->map, p.E_local, tile);
         const uint8_t* a_src = p.a_tiled + static_cast<size_t>(tile) * HB * TILE_BYTES;
         const uint8_t* b_src = p.w13p + (static_cast<size_t>(e) * G1_NT + j) * HB * G1_B_BYTES;
         for (int kb = 0; kb < HB; ++kb, ++it) {
@@ -269,7 +286,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(Gemm1Args p
     uint32_t it = 0, unit_no = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++unit_no) {
       const int tile = u / G1_NT, j = u % G1_NT;
-      const int e = checked_expert(p.tile_expert[tile], p.E_local);
+      const int e = tile_expert(&ctl->map, p.E_local, tile);
       const float* sa_ptr = p.a_scale + static_cast<size_t>(tile) * HB * TILE_M + row;
       const float* sg_ptr = p.w13_scale + (static_cast<size_t>(e) * G1B + j) * HB;
       const float* su_ptr = p.w13_scale + (static_cast<size_t>(e) * G1B + G1_NT + j) * HB;

@@ -28,14 +28,13 @@ struct Gemm2Args {
   const float* c_scale;     // [tiles, 16, 128]
   const uint8_t* w2p;       // [E, 28, 16, 256, 128] SW128 (packed by pack_w2_kernel)
   const float* w2_scale;    // [E, 56, 16]
-  const int* tile_expert;   // [tiles]
-  const int* tile_rows;     // [tiles]
-  const int* tile_dense;    // [tiles]  dense route index of the tile's first row
-  const int* n_tiles;       // [1]
-  int tiles_max;            // capacity of the workspace tile arrays
-  int E_local;              // number of local experts (bounds of tile_expert)
-  const float* route_w;     // [tiles * 128]
-  float* partial;           // [routes, 7168]
+  const int* counts;        // [E_local] routes per local expert
+  int slots;                // slots per expert (row stride of route_w)
+  int tiles_max;            // capacity of the c_* tile arrays
+  int E_local;
+  const float* route_w;     // [E_local, slots] routing weight of each expert slot
+  float* partial;           // [routes, 7168] dense: route (e, slot) is row dense_base[e] + slot
+  int* dense_base;          // [E_local + 1] written by CTA 0 for the combine
 };
 
 constexpr int G2_STAGES = 3;
@@ -43,7 +42,7 @@ constexpr int G2_A_BYTES = TILE_BYTES;      // one of hi / lo
 constexpr int G2_B_BYTES = 2 * TILE_BYTES;  // 256 W2 rows x 128 K bytes
 constexpr int G2_STAGE_BYTES = 2 * G2_A_BYTES + G2_B_BYTES;
 constexpr int G2_THREADS = GEMM_THREADS;
-constexpr int G2_CTRL_BYTES = 1024;
+constexpr int G2_CTRL_BYTES = 4096;
 constexpr int G2_SMEM = G2_STAGES * G2_STAGE_BYTES + G2_CTRL_BYTES + 1024;
 
 struct G2Ctrl {
@@ -54,15 +53,20 @@ struct G2Ctrl {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
+  TileMap map;
 };
 static_assert(sizeof(G2Ctrl) <= G2_CTRL_BYTES, "control block too large");
 
-__global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(Gemm2Args p) {
+__global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __grid_constant__ Gemm2Args p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = align_1024(smem_raw);
   G2Ctrl* ctl = reinterpret_cast<G2Ctrl*>(smem + G2_STAGES * G2_STAGE_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int n_units = clamp_tiles(*p.n_tiles, p.tiles_max) * G2_NT;
+  if (warp == 0) build_tile_map(&ctl->map, p.counts, p.E_local, p.slots);
+  __syncthreads();
+  if (blockIdx.x == 0)
+    for (int e = threadIdx.x; e <= p.E_local; e += blockDim.x) p.dense_base[e] = ctl->map.dense_off[e];
+  const int n_units = clamp_tiles(ctl->map.tile_off[p.E_local], p.tiles_max) * G2_NT;
   if (static_cast<int>(blockIdx.x) >= n_units) return;
 
   if (threadIdx.x == 0) {
@@ -100,7 +104,7 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(Gemm2Args
       uint32_t it = 0;
       for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
         const int tile = u / G2_NT, nt = u % G2_NT;
-        const int e = checked_expert(p.tile_expert[tile], p.E_local);
+        const int e = tile_expert(&ctl->map, p.E_local, tile);
         const size_t a_off = static_cast<size_t>(tile) * IB * TILE_BYTES;
         const uint8_t* b_src = p.w2p + (static_cast<size_t>(e) * G2_NT + nt) * IB * G2_B_BYTES;
         for (int ib = 0; ib < IB; ++ib, ++it) {
@@ -185,7 +189,8 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(Gemm2Args
     uint32_t it = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
       const int tile = u / G2_NT, nt = u % G2_NT;
-      const int e = checked_expert(p.tile_expert[tile], p.E_local);
+      const TileInfo ti = locate(&ctl->map, p.counts, p.E_local, tile, p.slots);
+      const int e = ti.e;
       const float* cs_ptr = p.c_scale + static_cast<size_t>(tile) * IB * TILE_M + row;
       const float* ws0 = p.w2_scale + (static_cast<size_t>(e) * HB + 2 * nt) * IB;
       const float* ws1 = ws0 + IB;
@@ -208,9 +213,10 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(Gemm2Args
       }
       if (named_bar_or(1, 256, aborted)) break;
 
-      if (row < p.tile_rows[tile]) {
-        const float w = p.route_w[static_cast<size_t>(tile) * TILE_M + row];
-        float* base = p.partial + static_cast<size_t>(p.tile_dense[tile] + row) * H + nt * 256 + hf * 64;
+      if (row < ti.rows) {
+        const int slot = ti.m * TILE_M + row;
+        const float w = p.route_w[static_cast<size_t>(e) * p.slots + slot];
+        float* base = p.partial + static_cast<size_t>(ctl->map.dense_off[e] + slot) * H + nt * 256 + hf * 64;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
           float4* dst = reinterpret_cast<float4*>(base + h * 128);

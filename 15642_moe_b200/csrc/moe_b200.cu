@@ -3,8 +3,8 @@
  * declared in include/moe_b200.h.
  *
  * moe_forward pipeline (one stream, no host synchronisation):
- *   memset(counts) -> route_kernel -> dispatch_kernel -> gather_kernel
- *   -> gemm1_swiglu_kernel (tcgen05) -> gemm2_weighted_kernel (tcgen05) -> combine_kernel
+ *   memset(counts) -> route_kernel -> gather_kernel -> gemm1_swiglu_kernel (tcgen05)
+ *   -> gemm2_weighted_kernel (tcgen05) -> combine_kernel
  * replacing the reference's route_dispatch / stage1 / stage2 / bf16_convert launches
  * (kernels/moe.cu:842-897).
  */
@@ -166,21 +166,20 @@ size_t moe_forward_workspace_bytes(int T, int E_local) {
 int moe_workspace_layout(int T, int E_local, size_t* offsets, int n) {
   if (T < 0 || E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "bad T or E_local");
   const Workspace w = make_workspace(T, E_local);
-  const size_t v[18] = {w.counts,     w.n_tiles,     w.topk_idx,    w.topk_w,  w.token_nr,
-                        w.token_row,  w.tile_expert, w.tile_rows,   w.tile_dense, w.route_token,
-                        w.route_w,    w.a_tiled,     w.a_scale,     w.c_hi,    w.c_lo,
-                        w.c_scale,    w.partial,     w.total};
-  for (int i = 0; i < n && i < 18; ++i) offsets[i] = v[i];
-  return 18;
+  const size_t v[15] = {w.counts,  w.dense_base, w.topk_idx, w.topk_w,  w.token_nr,
+                        w.token_route, w.route_token, w.route_w, w.a_tiled, w.a_scale,
+                        w.c_hi,    w.c_lo,       w.c_scale,  w.partial, w.total};
+  for (int i = 0; i < n && i < 15; ++i) offsets[i] = v[i];
+  return 15;
 }
 
 }  // extern "C"
 
 namespace {
 
-// The forward pipeline; when `events` is non-null, events[0..6] are recorded on the stream
-// before the first launch and after each of the six kernels (route, dispatch, gather, gemm1,
-// gemm2, combine).
+// The forward pipeline; when `events` is non-null, events[0..5] are recorded on the stream
+// before the first launch and after each of the five kernels (route, gather, gemm1, gemm2,
+// combine).
 int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_packed,
                  const float* w13_scale, const void* w2_packed, const float* w2_scale,
                  const float* logits, const float* bias, float routed_scaling_factor,
@@ -189,6 +188,7 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   if (T < 0) return fail(MOE_ERR_INVALID, "hidden must be [T, 7168]");
   if (E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "W13_packed must be [E_local, ...] with 1 <= E_local <= 256");
   if (T == 0) return MOE_OK;
+  if (T > MAX_TOKENS) return fail(MOE_ERR_INVALID, "moe_forward: T must be at most 65536");
   if (!hidden || !hidden_scale || !w13_packed || !w13_scale || !w2_packed || !w2_scale || !logits ||
       !bias || !out_bf16 || !workspace)
     return fail(MOE_ERR_INVALID, "moe_forward: null pointer argument");
@@ -204,22 +204,24 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   uint8_t* W = static_cast<uint8_t*>(workspace);
   int* counts = reinterpret_cast<int*>(W + ws.counts);
-  int* n_tiles = reinterpret_cast<int*>(W + ws.n_tiles);
+  int* dense_base = reinterpret_cast<int*>(W + ws.dense_base);
   int* topk_idx = reinterpret_cast<int*>(W + ws.topk_idx);
   float* topk_w = reinterpret_cast<float*>(W + ws.topk_w);
   int* token_nr = reinterpret_cast<int*>(W + ws.token_nr);
-  int* token_row = reinterpret_cast<int*>(W + ws.token_row);
-  int* tile_expert = reinterpret_cast<int*>(W + ws.tile_expert);
-  int* tile_rows = reinterpret_cast<int*>(W + ws.tile_rows);
-  int* tile_dense = reinterpret_cast<int*>(W + ws.tile_dense);
+  int* token_route = reinterpret_cast<int*>(W + ws.token_route);
   int* route_token = reinterpret_cast<int*>(W + ws.route_token);
   float* route_w = reinterpret_cast<float*>(W + ws.route_w);
-  uint8_t* a_tiled = W + ws.a_tiled;
-  float* a_scale = reinterpret_cast<float*>(W + ws.a_scale);
   uint8_t* c_hi = W + ws.c_hi;
   uint8_t* c_lo = W + ws.c_lo;
   float* c_scale = reinterpret_cast<float*>(W + ws.c_scale);
   float* partial = reinterpret_cast<float*>(W + ws.partial);
+
+  uint8_t* a_tiled = W + ws.a_tiled;
+  float* a_scale = reinterpret_cast<float*>(W + ws.a_scale);
+  Gemm1Args g1{a_tiled, a_scale, static_cast<const uint8_t*>(w13_packed), w13_scale, counts, T,
+               ws.tiles_max, E_local, c_hi, c_lo, c_scale};
+  Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, counts, T,
+               ws.tiles_max, E_local, route_w, partial, dense_base};
 
   auto mark = [&](int i) {
     if (events != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
@@ -227,32 +229,23 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   mark(0);
   if (int rc = cuda_check(cudaMemsetAsync(counts, 0, sizeof(int) * E_local, st), "memset counts")) return rc;
   route_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, routed_scaling_factor, local_expert_offset,
-                                            E_local, topk_idx, topk_w, counts, token_nr);
+                                            E_local, topk_idx, topk_w, counts, token_nr, token_route,
+                                            route_token, route_w);
   mark(1);
-  dispatch_kernel<<<E_local, 1024, 0, st>>>(topk_idx, topk_w, counts, T, E_local, local_expert_offset,
-                                            n_tiles, tile_expert, tile_rows, tile_dense, route_token,
-                                            route_w, token_row);
+  const size_t route_max = static_cast<size_t>(T) * (E_local < TOP_K ? E_local : TOP_K);
+  gather_kernel<<<grid_for(route_max, 8, d->num_sms * 8), 256, 0, st>>>(
+      static_cast<const uint8_t*>(hidden), hidden_scale, T, counts, E_local, route_token,
+      ws.tiles_max, a_tiled, a_scale);
   mark(2);
-  gather_kernel<<<grid_for(static_cast<size_t>(ws.tiles_max) * TILE_M, 8, d->num_sms * 8), 256, 0, st>>>(
-      static_cast<const uint8_t*>(hidden), hidden_scale, T, n_tiles, ws.tiles_max, route_token, a_tiled,
-      a_scale);
-  mark(3);
-
-  Gemm1Args g1{a_tiled, a_scale, static_cast<const uint8_t*>(w13_packed), w13_scale, tile_expert,
-               n_tiles, ws.tiles_max, E_local, c_hi, c_lo, c_scale};
   const int g1_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G1_NT, 1, d->num_sms);
   gemm1_swiglu_kernel<<<g1_grid, G1_THREADS, G1_SMEM, st>>>(g1);
-  mark(4);
-
-  Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, tile_expert,
-               tile_rows, tile_dense, n_tiles, ws.tiles_max, E_local, route_w, partial};
+  mark(3);
   const int g2_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G2_NT, 1, d->num_sms);
   gemm2_weighted_kernel<<<g2_grid, G2_THREADS, G2_SMEM, st>>>(g2);
+  mark(4);
+  combine_kernel<<<T, COMBINE_THREADS, 0, st>>>(partial, token_nr, token_route, dense_base, T,
+                                                static_cast<__nv_bfloat16*>(out_bf16));
   mark(5);
-
-  combine_kernel<<<T, COMBINE_THREADS, 0, st>>>(partial, token_nr, token_row, T,
-                                    static_cast<__nv_bfloat16*>(out_bf16));
-  mark(6);
   return cuda_check(cudaGetLastError(), "moe_forward launch");
 }
 
@@ -313,7 +306,8 @@ int moe_route(const float* logits, const float* bias, float routed_scaling_facto
   if (!logits || !bias || !topk_idx || !topk_w) return fail(MOE_ERR_INVALID, "moe_route: null pointer argument");
   if (!aligned16(logits) || !aligned16(bias)) return fail(MOE_ERR_INVALID, "moe_route: logits and bias must be 16-byte aligned");
   route_kernel<<<(T + 7) / 8, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-      logits, bias, T, routed_scaling_factor, 0, 0, topk_idx, topk_w, nullptr, nullptr);
+      logits, bias, T, routed_scaling_factor, 0, 0, topk_idx, topk_w, nullptr, nullptr, nullptr,
+      nullptr, nullptr);
   return cuda_check(cudaGetLastError(), "route_kernel launch");
 }
 

@@ -28,6 +28,7 @@ constexpr int HB = H / BLK;      // 56 hidden blocks
 constexpr int IB = I / BLK;      // 16 intermediate blocks
 constexpr int G1B = G1N / BLK;   // 32 GEMM1 output blocks
 
+constexpr int MAX_TOKENS = 65536;         // a route's slot is packed in 16 bits
 constexpr int TILE_M = 128;              // routed rows per tile (UMMA M)
 constexpr int TILE_BYTES = 128 * 128;    // one 128-row x 128-byte swizzled K block
 constexpr int G1_NT = I / BLK;           // 16 GEMM1 column tiles (128 X1 + 128 X2 rows each)
@@ -328,18 +329,15 @@ __device__ __forceinline__ uint8_t* align_1024(uint8_t* p) {
 // Workspace layout of one moe_forward call (all offsets 1024-byte aligned).
 // ------------------------------------------------------------------------------------------
 struct Workspace {
-  size_t counts;       // int32 [E_local]              routes per local expert
-  size_t n_tiles;      // int32 [1]                    active 128-row tiles
+  size_t counts;       // int32 [E_local]              routes per local expert (zeroed per call)
+  size_t dense_base;   // int32 [E_local + 1]          routes of experts < e (written by GEMM2)
   size_t topk_idx;     // int32 [T, 8]                 selected global experts
   size_t topk_w;       // fp32  [T, 8]                 routing weights
   size_t token_nr;     // int32 [T]                    local routes per token
-  size_t token_row;    // int32 [T, 8]                 routed row of each local route
-  size_t tile_expert;  // int32 [tiles_max]            local expert of each tile
-  size_t tile_rows;    // int32 [tiles_max]            valid rows of each tile
-  size_t tile_dense;   // int32 [tiles_max]            dense route index of each tile's row 0
-  size_t route_token;  // int32 [tiles_max*128]        token of each routed row (-1 = pad)
-  size_t route_w;      // fp32  [tiles_max*128]        routing weight of each routed row
-  size_t a_tiled;      // u8    [tiles_max, 56, 128, 128] gathered hidden rows, SW128 tiles
+  size_t token_route;  // int32 [T, 8]                 (le << 16 | slot), ascending le
+  size_t route_token;  // int32 [E_local, T]           token of each expert's slot
+  size_t route_w;      // fp32  [E_local, T]           routing weight of each expert's slot
+  size_t a_tiled;      // u8    [tiles_max, 56, 128, 128] routed hidden rows, SW128 tile images
   size_t a_scale;      // fp32  [tiles_max, 56, 128]   their per-128 block scales
   size_t c_hi;         // u8    [tiles_max, 16, 128, 128] SwiGLU output, e4m3 high part
   size_t c_lo;         // u8    [tiles_max, 16, 128, 128] e4m3 residual
@@ -367,17 +365,15 @@ inline Workspace make_workspace(int T, int E_local) {
     off = ws_align(off + bytes);
     return o;
   };
-  w.counts = take(sizeof(int) * (E_local > 0 ? E_local : 1));
-  w.n_tiles = take(sizeof(int));
+  const size_t e = static_cast<size_t>(E_local > 0 ? E_local : 1);
+  w.counts = take(sizeof(int) * e);
+  w.dense_base = take(sizeof(int) * (e + 1));
   w.topk_idx = take(sizeof(int) * TOP_K * static_cast<size_t>(T));
   w.topk_w = take(sizeof(float) * TOP_K * static_cast<size_t>(T));
   w.token_nr = take(sizeof(int) * static_cast<size_t>(T));
-  w.token_row = take(sizeof(int) * TOP_K * static_cast<size_t>(T));
-  w.tile_expert = take(sizeof(int) * tiles);
-  w.tile_rows = take(sizeof(int) * tiles);
-  w.tile_dense = take(sizeof(int) * tiles);
-  w.route_token = take(sizeof(int) * tiles * TILE_M);
-  w.route_w = take(sizeof(float) * tiles * TILE_M);
+  w.token_route = take(sizeof(int) * TOP_K * static_cast<size_t>(T));
+  w.route_token = take(sizeof(int) * e * static_cast<size_t>(T));
+  w.route_w = take(sizeof(float) * e * static_cast<size_t>(T));
   w.a_tiled = take(tiles * HB * TILE_BYTES);
   w.a_scale = take(sizeof(float) * tiles * HB * TILE_M);
   w.c_hi = take(tiles * IB * TILE_BYTES);
@@ -386,6 +382,71 @@ inline Workspace make_workspace(int T, int E_local) {
   w.partial = take(sizeof(float) * static_cast<size_t>(T) * kmax * H);
   w.total = off;
   return w;
+}
+
+// ------------------------------------------------------------------------------------------
+// Expert tile map. From the per-expert route counts (each expert's rows padded to 128-row
+// tiles, experts in ascending order): tile_off[e] = first tile of expert e, dense_off[e] =
+// number of routes of experts < e. Entry [E_local] holds the totals.
+// ------------------------------------------------------------------------------------------
+struct TileMap {
+  int tile_off[E_GLOBAL + 1];
+  int dense_off[E_GLOBAL + 1];
+};
+
+// Built by one full warp; the caller synchronises before use. A count outside [0, cap] is
+// reported and clamped, so a corrupted count can never address past the workspace.
+__device__ __forceinline__ void build_tile_map(TileMap* tm, const int* __restrict__ counts,
+                                               int E_local, int cap) {
+  const int lane = threadIdx.x & 31;
+  int c[8], tiles = 0, rows = 0;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane * 8 + i;
+    int v = e < E_local ? counts[e] : 0;
+    if (v < 0 || v > cap) {
+      report_status(ST_BAD_INDEX);
+      v = v < 0 ? 0 : cap;
+    }
+    c[i] = v;
+    tiles += (v + TILE_M - 1) / TILE_M;
+    rows += v;
+  }
+  int t_incl = tiles, r_incl = rows;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int tn = __shfl_up_sync(0xffffffffu, t_incl, o);
+    const int rn = __shfl_up_sync(0xffffffffu, r_incl, o);
+    if (lane >= o) {
+      t_incl += tn;
+      r_incl += rn;
+    }
+  }
+  int t = t_incl - tiles, r = r_incl - rows;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const int e = lane * 8 + i;
+    if (e <= E_local) {
+      tm->tile_off[e] = t;
+      tm->dense_off[e] = r;
+    }
+    t += (c[i] + TILE_M - 1) / TILE_M;
+    r += c[i];
+  }
+  if (lane == 31 && E_local == E_GLOBAL) {
+    tm->tile_off[E_GLOBAL] = t;
+    tm->dense_off[E_GLOBAL] = r;
+  }
+}
+
+// Expert of tile t: the e with tile_off[e] <= t < tile_off[e + 1] (empty experts own no tile).
+__device__ __forceinline__ int tile_expert(const TileMap* tm, int E_local, int t) {
+  int lo = 0, hi = E_local;  // invariant: tile_off[lo] <= t < tile_off[hi]
+  while (hi - lo > 1) {
+    const int mid = (lo + hi) >> 1;
+    if (tm->tile_off[mid] <= t) lo = mid; else hi = mid;
+  }
+  return lo;
 }
 
 }  // namespace moe

@@ -1,13 +1,18 @@
 /*
- * Routing, local dispatch, row gather and the final combine of the MoE forward.
+ * Routing and the final combine of the MoE forward.
  *
- *   route_kernel     no-aux-loss grouped top-k routing (reference/moe_ref.py:82-107)
- *   dispatch_kernel  per-local-expert compaction into 128-row tiles, rows in token order
- *                    (the selection step of reference/moe_ref.py:110-124)
- *   gather_kernel    copies the routed FP8 hidden rows into K-major SW128 tiles
+ *   route_kernel     no-aux-loss grouped top-k routing (reference/moe_ref.py:82-107); every
+ *                    local (token, expert) pair claims a slot in its expert's row list with one
+ *                    atomic, which replaces the per-expert selection of moe_ref.py:110-124
+ *   gather_kernel    copies each routed FP8 hidden row (and its 56 scales) into its expert's
+ *                    128-row tile image, K-major with the 128-byte swizzle
  *                    (the index_select of reference/moe_ref.py:124)
  *   combine_kernel   per-token sum of the weighted expert outputs in ascending expert
  *                    order, one bf16 rounding (reference/moe_ref.py:133-136)
+ *
+ * The slot order inside an expert's list depends on atomic timing, but no result does: every
+ * row of the expert GEMMs is computed independently of the other rows, and the combine adds a
+ * token's contributions in ascending expert order.
  */
 #pragma once
 #include "moe_common.cuh"
@@ -27,13 +32,20 @@ __device__ __forceinline__ bool better(float v, int i, float ov, int oi) {
 }
 
 // One warp per token; lane l owns experts 8l..8l+7, so a group of 32 experts is four lanes.
+// Outputs: topk_idx / topk_w [T, 8] in selection order. For the local picks (global expert g
+// with 0 <= le = g - local_offset < E_local), when `counts` is given: counts[le] (atomic),
+// route_token[le * T + slot] = t, route_w[le * T + slot] = weight, and the token's own list
+// token_route[t * 8 + k] = (le << 16) | slot in ascending le, token_nr[t] = its length.
 __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits,
                                                     const float* __restrict__ bias, int T,
                                                     float rsf, int local_offset, int E_local,
                                                     int* __restrict__ topk_idx,
                                                     float* __restrict__ topk_w,
                                                     int* __restrict__ counts,
-                                                    int* __restrict__ token_nr) {
+                                                    int* __restrict__ token_nr,
+                                                    int* __restrict__ token_route,
+                                                    int* __restrict__ route_token,
+                                                    float* __restrict__ route_w) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -144,137 +156,73 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
   int nlocal = 0;
 #pragma unroll
   for (int k = 0; k < TOP_K; ++k) {
-    int le = sel_idx[k] - local_offset;
-    bool local = le >= 0 && le < E_local;
-    nlocal += local ? 1 : 0;
+    const int le = sel_idx[k] - local_offset;
+    nlocal += (le >= 0 && le < E_local) ? 1 : 0;
+  }
+#pragma unroll
+  for (int k = 0; k < TOP_K; ++k) {
     if (lane == k) {
+      const float w = __fmul_rn(__fdiv_rn(sel_s[k], wsum), rsf);
       topk_idx[static_cast<size_t>(t) * TOP_K + k] = sel_idx[k];
-      topk_w[static_cast<size_t>(t) * TOP_K + k] = __fmul_rn(__fdiv_rn(sel_s[k], wsum), rsf);
-      if (local) atomicAdd(&counts[le], 1);
+      topk_w[static_cast<size_t>(t) * TOP_K + k] = w;
+      const int le = sel_idx[k] - local_offset;
+      if (counts != nullptr && le >= 0 && le < E_local) {
+        const int slot = atomicAdd(&counts[le], 1);
+        route_token[static_cast<size_t>(le) * T + slot] = t;
+        route_w[static_cast<size_t>(le) * T + slot] = w;
+        // Position in the token's list: local picks with a lower expert id come first.
+        int pos = 0;
+#pragma unroll
+        for (int j = 0; j < TOP_K; ++j) {
+          const int lj = sel_idx[j] - local_offset;
+          pos += (lj >= 0 && lj < le) ? 1 : 0;
+        }
+        token_route[static_cast<size_t>(t) * TOP_K + pos] = (le << 16) | slot;
+      }
     }
   }
   if (lane == 0 && token_nr != nullptr) token_nr[t] = nlocal;
 }
 
-// One CTA per local expert: finds the expert's tokens in token order and lays them out as
-// routed rows of its 128-row tiles. Tile offsets and the dense row base (index of the expert's
-// first route among all local routes, used for the expert-output rows) come from the counts.
-__global__ void __launch_bounds__(1024) dispatch_kernel(
-    const int* __restrict__ topk_idx, const float* __restrict__ topk_w,
-    const int* __restrict__ counts, int T, int E_local, int local_offset, int* __restrict__ n_tiles,
-    int* __restrict__ tile_expert, int* __restrict__ tile_rows, int* __restrict__ tile_dense,
-    int* __restrict__ route_token, float* __restrict__ route_w, int* __restrict__ token_row) {
-  __shared__ int s_cnt[E_GLOBAL];
-  __shared__ int s_off, s_base, s_running, s_total;
-  __shared__ int warp_pre[32];
-  const int e = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-  if (tid < E_local) s_cnt[tid] = counts[tid];
-  __syncthreads();
-  if (tid == 0) {
-    int off = 0, base = 0;
-    for (int i = 0; i < e; ++i) {
-      off += (s_cnt[i] + TILE_M - 1) / TILE_M;
-      base += s_cnt[i];
-    }
-    s_off = off;
-    s_base = base;
-    s_running = 0;
-    if (e == E_local - 1) *n_tiles = off + (s_cnt[e] + TILE_M - 1) / TILE_M;
-  }
-  __syncthreads();
-  const int off = s_off, cnt = s_cnt[e], dense0 = s_base;
-  const int nt = (cnt + TILE_M - 1) / TILE_M;
-  for (int i = tid; i < nt; i += blockDim.x) {
-    tile_expert[off + i] = e;
-    tile_rows[off + i] = min(TILE_M, cnt - TILE_M * i);
-    tile_dense[off + i] = dense0 + TILE_M * i;
-  }
-  const int ge = local_offset + e;
-  const size_t row0 = static_cast<size_t>(off) * TILE_M;
-
-  for (int base = 0; base < T; base += blockDim.x) {
-    const int t = base + tid;
-    int flag = 0, kslot = 0;
-    float w = 0.0f;
-    if (t < T) {
-#pragma unroll
-      for (int k = 0; k < TOP_K; ++k) {
-        int gk = topk_idx[static_cast<size_t>(t) * TOP_K + k];
-        if (gk == ge) {
-          flag = 1;
-          w = topk_w[static_cast<size_t>(t) * TOP_K + k];
-        } else if (gk >= local_offset && gk < ge) {
-          ++kslot;
-        }
-      }
-    }
-    const unsigned bal = __ballot_sync(0xffffffffu, flag);
-    const int pre = __popc(bal & ((1u << lane) - 1u));
-    if (lane == 0) warp_pre[wid] = __popc(bal);
-    __syncthreads();
-    if (wid == 0) {
-      int v = lane < (blockDim.x >> 5) ? warp_pre[lane] : 0;
-      int incl = v;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        int n = __shfl_up_sync(0xffffffffu, incl, o);
-        if (lane >= o) incl += n;
-      }
-      warp_pre[lane] = incl - v;
-      if (lane == 31) s_total = incl;
-    }
-    __syncthreads();
-    if (flag) {
-      const int slot = s_running + warp_pre[wid] + pre;
-      if (slot < cnt) {
-        const size_t row = row0 + slot;
-        route_token[row] = t;
-        route_w[row] = w;
-        token_row[static_cast<size_t>(t) * TOP_K + kslot] = dense0 + slot;
-      } else {
-        report_status(ST_BAD_INDEX);
-      }
-    }
-    __syncthreads();
-    if (tid == 0) s_running += s_total;
-    __syncthreads();
-  }
-  if (tid == 0 && s_running != cnt) report_status(ST_BAD_INDEX);
-  for (int r = cnt + tid; r < nt * TILE_M; r += blockDim.x) {
-    route_token[row0 + r] = -1;
-    route_w[row0 + r] = 0.0f;
-  }
-}
-
-// One warp per routed row: copies the FP8 hidden row of its token into the 56 K-major
-// 128B-swizzled 16 KB tiles of its 128-row tile, and its 56 block scales. Pad rows are zero.
+// One warp per local route (dense index d over all experts' slot lists): the route's tile row
+// is tile_off[e] * 128 + slot. Rows of a tile past its expert's last route are not written;
+// every row of the expert GEMMs is independent and those rows' results are never stored.
 __global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__ hidden,
                                                      const float* __restrict__ hidden_scale, int T,
-                                                     const int* __restrict__ n_tiles,
-                                                     int tiles_max,
+                                                     const int* __restrict__ counts, int E_local,
                                                      const int* __restrict__ route_token,
-                                                     uint8_t* __restrict__ a_tiled,
+                                                     int tiles_max, uint8_t* __restrict__ a_tiled,
                                                      float* __restrict__ a_scale) {
-  const int nrows = clamp_tiles(*n_tiles, tiles_max) * TILE_M;
+  __shared__ TileMap map;
+  if (threadIdx.x < 32) build_tile_map(&map, counts, E_local, T);
+  __syncthreads();
+  const int routes = map.dense_off[E_local];
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
-  for (int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; row < nrows; row += warps) {
-    const int tile = row >> 7, r = row & 127;
-    const int tok = route_token[row];
-    const bool ok = tok >= 0 && tok < T;
-    const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(ok ? tok : 0) * H);
+  for (int d = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; d < routes; d += warps) {
+    int lo = 0, hi = E_local;  // expert e with dense_off[e] <= d < dense_off[e + 1]
+    while (hi - lo > 1) {
+      const int mid = (lo + hi) >> 1;
+      if (map.dense_off[mid] <= d) lo = mid; else hi = mid;
+    }
+    const int slot = d - map.dense_off[lo];
+    const int tile = map.tile_off[lo] + slot / TILE_M, r = slot % TILE_M;
+    const int tok = route_token[static_cast<size_t>(lo) * T + slot];
+    if (tile >= tiles_max || tok < 0 || tok >= T) {
+      report_status(ST_BAD_INDEX);
+      continue;
+    }
+    const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(tok) * H);
     uint8_t* dst = a_tiled + static_cast<size_t>(tile) * HB * TILE_BYTES;
 #pragma unroll 2
     for (int q = lane; q < H / 16; q += 32) {
-      uint4 v = ok ? __ldg(src + q) : make_uint4(0u, 0u, 0u, 0u);
       const int kb = q >> 3, c = q & 7;
       *reinterpret_cast<uint4*>(dst + static_cast<size_t>(kb) * TILE_BYTES + r * 128 +
-                                ((c ^ (r & 7)) << 4)) = v;
+                                ((c ^ (r & 7)) << 4)) = __ldg(src + q);
     }
     for (int kb = lane; kb < HB; kb += 32)
       a_scale[(static_cast<size_t>(tile) * HB + kb) * TILE_M + r] =
-          ok ? __ldg(hidden_scale + static_cast<size_t>(kb) * T + tok) : 0.0f;
+          __ldg(hidden_scale + static_cast<size_t>(kb) * T + tok);
   }
 }
 
@@ -287,9 +235,12 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 
 // One CTA per token: out[t] = bf16( sum over its local routes, ascending expert order,
 // of the weighted expert outputs ), starting from +0 like the reference's zero tensor.
+// dense_base[le] = number of local routes of experts < le (written by the GEMM2 kernel), so
+// route (le, slot) of a token is row dense_base[le] + slot of `partial`.
 __global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(const float* __restrict__ partial,
                                                                   const int* __restrict__ token_nr,
-                                                                  const int* __restrict__ token_row,
+                                                                  const int* __restrict__ token_route,
+                                                                  const int* __restrict__ dense_base,
                                                                   int T,
                                                                   __nv_bfloat16* __restrict__ out) {
   const int t = blockIdx.x;
@@ -302,8 +253,9 @@ __global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(const float* _
 #pragma unroll
   for (int k = 0; k < TOP_K; ++k) {
     if (k < n) {
-      const float4* src = reinterpret_cast<const float4*>(
-          partial + static_cast<size_t>(token_row[static_cast<size_t>(t) * TOP_K + k]) * H + c0);
+      const int packed = token_route[static_cast<size_t>(t) * TOP_K + k];
+      const int row = dense_base[packed >> 16] + (packed & 0xFFFF);
+      const float4* src = reinterpret_cast<const float4*>(partial + static_cast<size_t>(row) * H + c0);
       float4 p[4];
 #pragma unroll
       for (int j = 0; j < 4; ++j) p[j] = __ldcs(src + j);

@@ -5,7 +5,7 @@
 
 Workload at N=1: benchmark configuration 2 (T=4096 tokens, 32 local experts of 256,
 local_expert_offset 0; the prefill case the headline tokens/s is quoted on). Each step is one
-full moe_forward: route -> dispatch -> gather -> GEMM1+SwiGLU -> GEMM2 -> combine. The
+full moe_forward: route -> gather -> GEMM1+SwiGLU -> GEMM2 -> combine. The
 1.41 GB of FP8 expert weights exceed the 126 MB L2, so no flush is needed between steps.
 The decode case (configuration 1, T=64) is reported alongside as microseconds per layer.
 
@@ -42,7 +42,7 @@ W13_SCALE_BYTES = 32 * 56 * 4
 W2_SCALE_BYTES = 56 * 16 * 4
 FLOPS_G1_PER_ROUTE = 2 * 7168 * 4096
 FLOPS_G2_PER_ROUTE = 2 * 2048 * 7168
-STAGES = ["route", "dispatch", "gather", "gemm1_swiglu", "gemm2_weighted", "combine"]
+STAGES = ["route", "gather", "gemm1_swiglu", "gemm2_weighted", "combine"]
 
 
 def load_peaks() -> dict:
@@ -129,10 +129,9 @@ def kernel_work(rs: dict, T: int) -> dict:
                              + r * (2 * 2048 + 16 * 4), flops=r * FLOPS_G1_PER_ROUTE),
         "gemm2_weighted": dict(bytes=a * (W2_EXPERT_BYTES + W2_SCALE_BYTES) + r * (2 * 2048 + 16 * 4)
                                + r * 7168 * 4, flops=2 * r * FLOPS_G2_PER_ROUTE),
-        "gather": dict(bytes=r * (7168 + 56 * 4) * 2, flops=0),
         "combine": dict(bytes=r * 7168 * 4 + T * 7168 * 2, flops=0),
         "route": dict(bytes=T * 256 * 4 + T * 8 * 8, flops=0),
-        "dispatch": dict(bytes=T * 8 * 8, flops=0),
+        "gather": dict(bytes=r * (7168 + 56 * 4) * 2, flops=0),
     }
 
 
@@ -164,7 +163,7 @@ class Step:
         self.pkg._native.check(self.lib.moe_forward(*self.args))
 
     def profiled(self, events):
-        arr = (ctypes.c_void_p * 7)(*[e.cuda_event for e in events])
+        arr = (ctypes.c_void_p * (len(STAGES) + 1))(*[e.cuda_event for e in events])
         self.pkg._native.check(self.lib.moe_forward_profiled(*self.args, arr))
 
 
@@ -181,7 +180,7 @@ def time_steps(fn, steps: int) -> float:
 
 
 def stage_times(step: Step, reps: int) -> dict:
-    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(7)] for _ in range(reps)]
+    evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(STAGES) + 1)] for _ in range(reps)]
     for row in evs:          # torch creates the CUDA event on first record
         for ev in row:
             ev.record()
@@ -359,7 +358,7 @@ def bench_ours(args, rank, world, local_rank, dist):
                 "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
                 "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
                 "ms_per_step": round(e2e["ms_per_step"], 4)},
-        "gpu_launches": 6 * args.steps,
+        "gpu_launches": len(STAGES) * args.steps,
         "clocks": clocks,
         "device_status": status,
     }

@@ -72,6 +72,7 @@ size_t moe_forward_workspace_bytes(int T, int E_local);
  *   routed_scaling_factor, local_expert_offset: as reference/moe_ref.py:14-15
  *   out_bf16      bf16 [T, 7168]          (written completely; tokens without a local
  *                                          expert get zeros)
+ *   T             0 <= T <= 65536
  * All device pointers 16-byte aligned. Asynchronous; no host synchronisation. */
 int moe_forward(const void* hidden, const float* hidden_scale, const void* w13_packed,
                 const float* w13_scale, const void* w2_packed, const float* w2_scale,
@@ -104,9 +105,9 @@ int moe_forward_noalloc(const void* hidden, const float* hidden_scale, const voi
                         const float* logits, const float* bias, float routed_scaling_factor,
                         int local_expert_offset, int T, int E_local, void* out_bf16, void* stream);
 
-/* moe_forward that also records events[0..6] (cudaEvent_t) on `stream`: before the first
- * launch and after each of its six kernels (route, dispatch, gather, gemm1, gemm2,
- * combine), for per-kernel timing. No reference counterpart (instrumentation only). */
+/* moe_forward that also records events[0..5] (cudaEvent_t) on `stream`: before the first
+ * launch and after each of its five kernels (route, gather, gemm1, gemm2, combine), for
+ * per-kernel timing. No reference counterpart (instrumentation only). */
 int moe_forward_profiled(const void* hidden, const float* hidden_scale, const void* w13_packed,
                          const float* w13_scale, const void* w2_packed, const float* w2_scale,
                          const float* logits, const float* bias, float routed_scaling_factor,
@@ -122,9 +123,9 @@ int moe_route(const float* logits, const float* bias, float routed_scaling_facto
               int* topk_idx, float* topk_w, void* stream);
 
 /* Byte offsets of the internal workspace regions for (T, E_local), in this order:
- * counts, n_tiles, topk_idx, topk_w, token_nr, token_row, tile_expert, tile_rows,
- * tile_dense, route_token, route_w, a_tiled, a_scale, c_hi, c_lo, c_scale, partial, total.
- * Writes min(n, 18) values; returns the number of regions (18). For tests and tooling. */
+ * counts, dense_base, topk_idx, topk_w, token_nr, token_route, route_token, route_w, a_tiled,
+ * a_scale, c_hi, c_lo, c_scale, partial, total. Writes min(n, 15) values; returns the number of
+ * regions (15). For tests and tooling. */
 int moe_workspace_layout(int T, int E_local, size_t* offsets, int n);
 
 /* ---- Seeded synthetic inputs on the GPU (bit-identical to the CPU generator) ----

@@ -44,9 +44,11 @@ def test_sizes(pkg):
     assert offs == sorted(offs) and all(v % 1024 == 0 for v in offs)
     # expert outputs are stored densely, one fp32 row per local route (at most 8 per token)
     assert lay["partial"] + 64 * 8 * 7168 * 4 <= lay["total"]
-    # tiles are padded per expert: every token routed to 8 local experts, each tile partial
+    # SwiGLU tiles are padded per expert: every token routed to 8 local experts, each tile partial
     tiles = (64 * 8 + 32 * 127 + 127) // 128
-    assert lay["a_scale"] - lay["a_tiled"] >= tiles * 56 * 128 * 128
+    assert lay["c_lo"] - lay["c_hi"] >= tiles * 16 * 128 * 128
+    # per-expert slot lists hold up to T routes each
+    assert lay["route_w"] - lay["route_token"] >= 32 * 64 * 4
 
 
 def test_host_side_argument_errors(pkg):

@@ -89,39 +89,44 @@ def test_stages(pkg, oracle):
     npi = oracle.to_numpy_inputs(inp)
     idx, w = oracle.route(npi["routing_logits"], npi["routing_bias"], cfg.routed_scaling_factor)
 
-    # routing metadata
+    # routing metadata: per-expert slot lists (any order) and each token's ascending list
     counts = region(ws, lay, "counts", torch.int32, E)
     exp_counts = np.array([(idx == e).any(axis=1).sum() for e in range(E)])
     np.testing.assert_array_equal(counts, exp_counts)
-    n_tiles = int(region(ws, lay, "n_tiles", torch.int32, 1)[0])
-    assert n_tiles == int(sum((c + 127) // 128 for c in exp_counts))
-    tile_expert = region(ws, lay, "tile_expert", torch.int32, n_tiles)
-    route_token = region(ws, lay, "route_token", torch.int32, n_tiles * 128)
-    route_w = region(ws, lay, "route_w", torch.float32, n_tiles * 128)
-    t0 = 0
+    route_token = region(ws, lay, "route_token", torch.int32, E * T).reshape(E, T)
+    route_w = region(ws, lay, "route_w", torch.float32, E * T).reshape(E, T)
+    token_nr = region(ws, lay, "token_nr", torch.int32, T)
+    token_route = region(ws, lay, "token_route", torch.int32, T * 8).reshape(T, 8)
+    dense_base = region(ws, lay, "dense_base", torch.int32, E + 1)
+    np.testing.assert_array_equal(dense_base, np.concatenate([[0], np.cumsum(exp_counts)]))
     for e in range(E):
-        nt = (exp_counts[e] + 127) // 128
-        assert (tile_expert[t0:t0 + nt] == e).all()
-        rows = route_token[t0 * 128:(t0 + nt) * 128]
         toks = np.nonzero((idx == e).any(axis=1))[0]
-        np.testing.assert_array_equal(rows[:len(toks)], toks)
-        assert (rows[len(toks):] == -1).all()
-        wexp = np.array([w[t][idx[t] == e][0] for t in toks], np.float32)
-        np.testing.assert_array_equal(route_w[t0 * 128:t0 * 128 + len(toks)], wexp)
-        t0 += nt
+        got = route_token[e, :exp_counts[e]]
+        np.testing.assert_array_equal(np.sort(got), toks)
+        wexp = np.array([w[t][idx[t] == e][0] for t in got], np.float32)
+        np.testing.assert_array_equal(route_w[e, :exp_counts[e]], wexp)
+    for t in range(T):
+        local = sorted(int(g) for g in idx[t] if g < E)
+        assert token_nr[t] == len(local)
+        for k, g in enumerate(local):
+            le, slot = token_route[t, k] >> 16, token_route[t, k] & 0xFFFF
+            assert le == g and route_token[le, slot] == t
 
-    # gather: bit-exact FP8 rows in swizzled tiles
+    # gather: bit-exact FP8 rows and scales in the experts' swizzled tile images
+    n_tiles = int(sum((c + 127) // 128 for c in exp_counts))
     a = region(ws, lay, "a_tiled", torch.uint8, n_tiles * 56 * 128 * 128).reshape(n_tiles, 56, 128, 128)
     a = unswizzle(a).transpose(0, 2, 1, 3).reshape(n_tiles * 128, 7168)
-    hid = npi["hidden_states"]
-    valid = route_token >= 0
-    np.testing.assert_array_equal(a[valid], hid[route_token[valid]])
-    assert (a[~valid] == 0).all()
     asc = region(ws, lay, "a_scale", torch.float32, n_tiles * 56 * 128).reshape(n_tiles, 56, 128)
     asc = asc.transpose(0, 2, 1).reshape(n_tiles * 128, 56)
-    np.testing.assert_array_equal(asc[valid], npi["hidden_states_scale"].T[route_token[valid]])
+    t0 = 0
+    for e in range(E):
+        toks = route_token[e, :exp_counts[e]]
+        rows = t0 * 128 + np.arange(exp_counts[e])
+        np.testing.assert_array_equal(a[rows], npi["hidden_states"][toks])
+        np.testing.assert_array_equal(asc[rows], npi["hidden_states_scale"].T[toks])
+        t0 += (exp_counts[e] + 127) // 128
 
-    # GEMM1 + SwiGLU: C = scale * (hi + lo) vs the fp32 oracle, per (row, 128-block)
+    # GEMM1 + SwiGLU: C = scale * (hi + lo) vs the fp32 oracle
     A = oracle.dequant_hidden(npi["hidden_states"], npi["hidden_states_scale"])
     hi = unswizzle(region(ws, lay, "c_hi", torch.uint8, n_tiles * 16 * 128 * 128).reshape(n_tiles, 16, 128, 128))
     lo = unswizzle(region(ws, lay, "c_lo", torch.uint8, n_tiles * 16 * 128 * 128).reshape(n_tiles, 16, 128, 128))
@@ -130,18 +135,15 @@ def test_stages(pkg, oracle):
     cval = cval.transpose(0, 2, 1, 3).reshape(n_tiles * 128, 2048)
     routes = int(exp_counts.sum())
     partial = region(ws, lay, "partial", torch.float32, routes * 7168).reshape(routes, 7168)
-    tile_dense = region(ws, lay, "tile_dense", torch.int32, n_tiles)
-    dense_base = np.concatenate([[0], np.cumsum(exp_counts)[:-1]])
     t0 = 0
     worst_c, worst_o = 0.0, 0.0
     for e in range(E):
         nt = (exp_counts[e] + 127) // 128
         if nt == 0:
             continue
-        rows = np.arange(t0 * 128, t0 * 128 + exp_counts[e])
+        rows = np.arange(t0 * 128, t0 * 128 + exp_counts[e])      # tile rows = slots
         drows = dense_base[e] + np.arange(exp_counts[e])
-        assert tile_dense[t0] == dense_base[e]
-        toks = route_token[rows]
+        toks = route_token[e, :exp_counts[e]]
         W13 = oracle.dequant_block(npi["gemm1_weights"][e], npi["gemm1_weights_scale"][e])
         G1 = A[toks] @ W13.T
         C = (G1[:, 2048:] / (1.0 + np.exp(-G1[:, 2048:]))) * G1[:, :2048]
@@ -149,10 +151,22 @@ def test_stages(pkg, oracle):
         err = np.abs(cval[rows] - C).reshape(len(toks), 16, 128) / (blk_max + 1e-30)
         worst_c = max(worst_c, float(err.max()))
         W2 = oracle.dequant_block(npi["gemm2_weights"][e], npi["gemm2_weights_scale"][e])
-        Oe = (C @ W2.T) * route_w[rows][:, None]
+        Oe = (C @ W2.T) * route_w[e, :exp_counts[e]][:, None]
         rel = np.abs(partial[drows] - Oe).max(axis=1) / (np.abs(Oe).max(axis=1) + 1e-30)
         worst_o = max(worst_o, float(rel.max()))
         t0 += nt
     print("worst C block-relative err", worst_c, "worst partial row-relative err", worst_o)
     assert worst_c < 2.0 ** -7
     assert worst_o < 1e-2
+
+
+def test_forward_two_tile_experts(pkg, oracle):
+    """Skewed routing with T=1536: hot experts span several 128-row tiles (gather across tiles)."""
+    cfg = pkg.CONFIGS[4].with_(T=1536, E_local=32, seed=3)
+    inp = pkg.make_inputs(cfg, "cuda")
+    out, ws = forward_with_workspace(pkg, inp)
+    counts = region(ws, pkg.workspace_layout(cfg.T, 32), "counts", torch.int32, 32)
+    assert counts.max() > 256
+    ref = oracle.moe_forward(**oracle.to_numpy_inputs(inp))
+    r = oracle.check_tolerance(ref, out_bits(out), ATOL, RTOL)
+    assert r["bad"] == 0, r
