@@ -32,6 +32,9 @@ CUDA_SIGNATURES = {
     "moe_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                             c_void_p, c_float, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t,
                             c_void_p]),
+    "moe_forward_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                c_void_p, c_float, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t,
+                                c_void_p]),
     "moe_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_void_p,
                                     c_void_p]),
@@ -40,6 +43,18 @@ CUDA_SIGNATURES = {
                                      c_void_p, c_size_t, c_void_p, c_void_p]),
     "moe_route": (c_int, [c_void_p, c_void_p, c_float, c_int, c_void_p, c_void_p, c_void_p]),
     "moe_workspace_layout": (c_int, [c_int, c_int, c_size_t_p, c_int]),
+    "moe_ep_symmetric_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "moe_ep_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
+    "moe_ep_create": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(c_void_p), c_void_p]),
+    "moe_ep_connect": (c_int, [c_void_p, c_void_p]),
+    "moe_ep_destroy": (c_int, [c_void_p]),
+    "moe_ep_info": (c_int, [c_void_p, c_int_p]),
+    "moe_ep_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                               c_void_p, c_void_p, c_void_p, c_float, c_int, c_void_p, c_void_p,
+                               c_size_t, c_void_p]),
+    "moe_ep_forward_profiled": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                        c_void_p, c_void_p, c_void_p, c_float, c_int, c_void_p,
+                                        c_void_p, c_size_t, c_void_p, c_void_p]),
     "moe_synth_logits": (c_int, [c_void_p, c_uint64, c_int, c_int, c_void_p, c_void_p]),
     "moe_synth_bias": (c_int, [c_void_p, c_uint64, c_int, c_float, c_void_p, c_int, c_float,
                                c_void_p, c_void_p]),
@@ -99,6 +114,11 @@ def check(rc: int) -> None:
     if rc != 0:
         msg = cuda_lib().moe_last_error().decode(errors="replace")
         raise MoEError(msg or f"moe call failed with code {rc}")
+
+
+# Bits of the device status word (include/moe_b200.h).
+ST_TIMEOUT_PRODUCER, ST_TIMEOUT_MMA, ST_TIMEOUT_EPILOGUE, ST_BAD_INDEX, ST_EP_TIMEOUT = 1, 2, 4, 8, 16
+EP_HANDLE_BYTES = 64
 
 
 def device_status(reset: bool = True) -> int:

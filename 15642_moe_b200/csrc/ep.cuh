@@ -1,0 +1,259 @@
+/*
+ * Expert-parallel (EP) MoE layer: W ranks (one GPU each, W <= 8), rank r owns the global
+ * experts [r * E_rank, (r + 1) * E_rank) and holds its own T_r tokens. Token dispatch and the
+ * return of expert outputs are peer stores over NVLink issued by these kernels; the only
+ * host-side collective is the one-time exchange of CUDA IPC handles.
+ *
+ * Every rank owns one "symmetric" buffer with the same layout (EpLayout); each rank maps all
+ * W buffers (its own plus the peers' through CUDA IPC) and passes their addresses as EpPeers.
+ * A forward on rank r, epoch e (all ranks call it the same number of times):
+ *
+ *   route_kernel            top-8 of 256 for the own T_r tokens (topk only)
+ *   ep_dispatch_kernel      per token and owner rank d that it picked: its FP8 row and 56
+ *                           scales -> d.recv[r * T_max + t]; per pick a slot of d's expert
+ *                           list claimed with a system-scope atomic on d.counts, and the
+ *                           (row, weight, slot) records that d's gather / GEMM2 / combine read
+ *   ep_barrier_kernel       release flag d.arrive[r] = e on every d, acquire own arrive[*] >= e
+ *   gather, GEMM1, GEMM2    unchanged single-GPU kernels over the received rows
+ *                           (row index = src * T_max + t, W * T_max "tokens")
+ *   ep_combine_send_kernel  per received row: fp32 sum of its local routes in ascending
+ *                           expert order, stored unrounded to src.comb[r][t]
+ *   memset(own counts), ep_barrier_kernel on the `done` flags
+ *   ep_final_combine_kernel out[t] = bf16( sum over owners d ascending of comb[d][t] )
+ *
+ * The partials travel in fp32 so the layer keeps the reference's single bf16 rounding of an
+ * fp32 sum (moe_ref.py:110-136); rounding each owner's partial to bf16 first can move a
+ * result by more than the reference tolerance where partials of different owners cancel.
+ *
+ * Reuse of buffers across epochs is safe without double buffering: a source starts epoch
+ * e + 1's dispatch only after every owner signalled `done` for epoch e, which each owner does
+ * after its last read of epoch e's received data and after zeroing its counts; an owner
+ * writes epoch e + 1's comb rows only after every source signalled `arrive` for e + 1, which
+ * each source does after its final combine of epoch e.
+ *
+ * Waits are bounded (WAIT_LIMIT_NS); on timeout the barrier reports ST_EP_TIMEOUT and
+ * returns, and every consumer of peer-written metadata checks it before addressing memory.
+ * No load here uses TMA multicast; peers are read and written with plain loads and stores.
+ */
+#pragma once
+#include "route.cuh"
+
+namespace moe {
+
+constexpr int EP_MAX_RANKS = 8;
+
+struct EpLayout {
+  int world, t_max, e_rank, r_cap;  // r_cap = world * t_max received-row slots
+  size_t arrive, done, src_T, counts, recv_rows, recv_scale, route_token, route_w, tok_nr,
+      tok_route, comb, total;
+};
+
+// Byte offsets of the symmetric buffer (identical on every rank).
+//   arrive/done  u32 [8]             epoch flags, index = signalling rank
+//   src_T        int [8]             tokens each source sent this epoch
+//   counts       int [E_rank]        routes per local expert (claimed by remote atomics)
+//   recv_rows    u8  [r_cap, 7168]   received FP8 rows, row = src * t_max + t
+//   recv_scale   f32 [56, r_cap]     their scales, block-major like hidden_states_scale
+//   route_token  int [E_rank, r_cap] received row of each expert slot
+//   route_w      f32 [E_rank, r_cap] routing weight of each expert slot
+//   tok_nr       int [r_cap]         local routes of each received row
+//   tok_route    int [r_cap, 8]      (le << 16) | slot of those routes, ascending le
+//   comb         f32 [world, t_max, 7168]   returned partial sums, index = owner rank
+inline EpLayout make_ep_layout(int world, int t_max, int e_rank) {
+  EpLayout L{};
+  L.world = world;
+  L.t_max = t_max;
+  L.e_rank = e_rank;
+  L.r_cap = world * t_max;
+  const size_t rc = static_cast<size_t>(L.r_cap), e = static_cast<size_t>(e_rank);
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = ws_align(off + bytes);
+    return o;
+  };
+  L.arrive = take(sizeof(unsigned) * EP_MAX_RANKS);
+  L.done = take(sizeof(unsigned) * EP_MAX_RANKS);
+  L.src_T = take(sizeof(int) * EP_MAX_RANKS);
+  L.counts = take(sizeof(int) * e);
+  L.recv_rows = take(rc * H);
+  L.recv_scale = take(sizeof(float) * HB * rc);
+  L.route_token = take(sizeof(int) * e * rc);
+  L.route_w = take(sizeof(float) * e * rc);
+  L.tok_nr = take(sizeof(int) * rc);
+  L.tok_route = take(sizeof(int) * TOP_K * rc);
+  L.comb = take(sizeof(float) * rc * H);
+  L.total = off;
+  return L;
+}
+
+struct EpPeers {
+  uint8_t* base[EP_MAX_RANKS];  // symmetric buffer of each rank, mapped into this process
+};
+
+template <typename T_>
+__host__ __device__ __forceinline__ T_* ep_at(uint8_t* base, size_t off) {
+  return reinterpret_cast<T_*>(base + off);
+}
+
+// One warp per own token. Lanes 0-7 hold the token's picks; owner d = ge / E_rank (picks of
+// experts >= world * E_rank have no owner and are dropped, as moe_ref.py:115-116 drops
+// non-local experts).
+__global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant__ EpPeers peers, const __grid_constant__ EpLayout L, int rank, int T,
+                                                          const uint8_t* __restrict__ hidden,
+                                                          const float* __restrict__ hidden_scale,
+                                                          const int* __restrict__ topk_idx,
+                                                          const float* __restrict__ topk_w) {
+  if (blockIdx.x == 0 && threadIdx.x < L.world)
+    ep_at<int>(peers.base[threadIdx.x], L.src_T)[rank] = T;
+  const int lane = threadIdx.x & 31;
+  const int warps = (gridDim.x * blockDim.x) >> 5;
+  const int owned = L.world * L.e_rank;
+  for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < T; t += warps) {
+    const int ge = lane < TOP_K ? topk_idx[static_cast<size_t>(t) * TOP_K + lane] : -1;
+    const float w = lane < TOP_K ? topk_w[static_cast<size_t>(t) * TOP_K + lane] : 0.0f;
+    const int d = (ge >= 0 && ge < owned) ? ge / L.e_rank : -1;
+    int pos = 0, nd = 0;
+    unsigned mask = 0;
+#pragma unroll
+    for (int j = 0; j < TOP_K; ++j) {
+      const int gj = __shfl_sync(0xffffffffu, ge, j);
+      const int dj = __shfl_sync(0xffffffffu, d, j);
+      pos += (d >= 0 && dj == d && gj < ge) ? 1 : 0;
+      nd += (dj == lane) ? 1 : 0;
+      mask |= dj >= 0 ? (1u << dj) : 0u;
+    }
+    const int row = rank * L.t_max + t;
+    if (lane < L.world) ep_at<int>(peers.base[lane], L.tok_nr)[row] = nd;
+    if (d >= 0) {
+      uint8_t* pb = peers.base[d];
+      const int le = ge - d * L.e_rank;
+      const int slot = atomicAdd_system(ep_at<int>(pb, L.counts) + le, 1);
+      if (slot < L.r_cap) {
+        const size_t i = static_cast<size_t>(le) * L.r_cap + slot;
+        ep_at<int>(pb, L.route_token)[i] = row;
+        ep_at<float>(pb, L.route_w)[i] = w;
+        ep_at<int>(pb, L.tok_route)[static_cast<size_t>(row) * TOP_K + pos] = (le << 16) | slot;
+      } else {
+        report_status(ST_BAD_INDEX);
+      }
+    }
+    if (mask == 0) continue;
+    // The row is read once into registers and stored to every owner that needs it.
+    const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(t) * H);
+    uint4 v[H / 16 / 32];
+#pragma unroll
+    for (int i = 0; i < H / 16 / 32; ++i) v[i] = __ldg(src + lane + 32 * i);
+    float s0 = 0.0f, s1 = 0.0f;
+    if (lane < HB / 2) {
+      s0 = __ldg(hidden_scale + static_cast<size_t>(lane) * T + t);
+      s1 = __ldg(hidden_scale + static_cast<size_t>(lane + HB / 2) * T + t);
+    }
+    for (int dd = 0; dd < L.world; ++dd) {
+      if (!(mask & (1u << dd))) continue;
+      uint8_t* pb = peers.base[dd];
+      uint4* dst = reinterpret_cast<uint4*>(pb + L.recv_rows + static_cast<size_t>(row) * H);
+#pragma unroll
+      for (int i = 0; i < H / 16 / 32; ++i) dst[lane + 32 * i] = v[i];
+      if (lane < HB / 2) {
+        float* sc = ep_at<float>(pb, L.recv_scale);
+        sc[static_cast<size_t>(lane) * L.r_cap + row] = s0;
+        sc[static_cast<size_t>(lane + HB / 2) * L.r_cap + row] = s1;
+      }
+    }
+  }
+}
+
+// One warp: lane d < world publishes `epoch` into rank d's flag slot [rank] (after a
+// system-scope fence, so every store this rank issued before this kernel is visible first),
+// then lane j < world waits, bounded, until this rank's flag [j] reaches `epoch`.
+__global__ void __launch_bounds__(32) ep_barrier_kernel(const __grid_constant__ EpPeers peers, size_t flag_off, int rank,
+                                                        int world, unsigned epoch) {
+  const int lane = threadIdx.x;
+  if (lane < world) {
+    __threadfence_system();
+    st_release_sys(ep_at<unsigned>(peers.base[lane], flag_off) + rank, epoch);
+    const unsigned* f = ep_at<unsigned>(peers.base[rank], flag_off) + lane;
+    const unsigned long long t0 = globaltimer();
+    while (static_cast<int>(ld_acquire_sys(f) - epoch) < 0) {
+      if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+        report_status(ST_EP_TIMEOUT);
+        break;
+      }
+      __nanosleep(128);
+    }
+  }
+  __syncwarp();
+}
+
+// Grid-stride over the received rows (one CTA of 448 threads x 16 columns per row): the fp32
+// sum of the row's local routes in ascending expert order from +0, stored into the source
+// rank's comb[rank][t].
+__global__ void __launch_bounds__(COMBINE_THREADS) ep_combine_send_kernel(const __grid_constant__ EpPeers peers, const __grid_constant__ EpLayout L,
+                                                                          int rank,
+                                                                          const float* __restrict__ partial,
+                                                                          const int* __restrict__ dense_base) {
+  uint8_t* me = peers.base[rank];
+  const int* src_T = ep_at<int>(me, L.src_T);
+  const int* tok_nr = ep_at<int>(me, L.tok_nr);
+  const int* tok_route = ep_at<int>(me, L.tok_route);
+  const int c0 = threadIdx.x * 16;
+  for (int i = blockIdx.x; i < L.r_cap; i += gridDim.x) {
+    const int src = i / L.t_max, t = i - src * L.t_max;
+    int tn = src_T[src];
+    if (tn > L.t_max) {
+      if (threadIdx.x == 0) report_status(ST_BAD_INDEX);
+      tn = L.t_max;
+    }
+    if (t >= tn) continue;
+    const int n = tok_nr[i];
+    if (n <= 0) continue;
+    float acc[16];
+#pragma unroll
+    for (int k = 0; k < 16; ++k) acc[k] = 0.0f;
+    add_routes(acc, partial, tok_route + static_cast<size_t>(i) * TOP_K, n, dense_base, L.e_rank, c0);
+    float* dst = ep_at<float>(peers.base[src], L.comb) + (static_cast<size_t>(rank) * L.t_max + t) * H + c0;
+    store_f32x16(dst, acc);
+  }
+}
+
+__device__ __forceinline__ void add_f32x16(float (&acc)[16], const float* p) {
+  const float4* q = reinterpret_cast<const float4*>(p);
+  float4 v[4];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) v[j] = __ldcs(q + j);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) {
+    acc[4 * j + 0] = __fadd_rn(acc[4 * j + 0], v[j].x);
+    acc[4 * j + 1] = __fadd_rn(acc[4 * j + 1], v[j].y);
+    acc[4 * j + 2] = __fadd_rn(acc[4 * j + 2], v[j].z);
+    acc[4 * j + 3] = __fadd_rn(acc[4 * j + 3], v[j].w);
+  }
+}
+
+// One CTA per own token: out[t] = bf16( sum over the owners of its picks, ascending rank,
+// of comb[d][t] ) from +0; tokens whose picks have no owner get zeros.
+__global__ void __launch_bounds__(COMBINE_THREADS) ep_final_combine_kernel(const uint8_t* __restrict__ me,
+                                                                           EpLayout L, int T,
+                                                                           const int* __restrict__ topk_idx,
+                                                                           __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const int owned = L.world * L.e_rank;
+  unsigned mask = 0;
+#pragma unroll
+  for (int k = 0; k < TOP_K; ++k) {
+    const int ge = topk_idx[static_cast<size_t>(t) * TOP_K + k];
+    if (ge >= 0 && ge < owned) mask |= 1u << (ge / L.e_rank);
+  }
+  const int c0 = threadIdx.x * 16;
+  const float* comb = reinterpret_cast<const float*>(me + L.comb);
+  float acc[16];
+#pragma unroll
+  for (int k = 0; k < 16; ++k) acc[k] = 0.0f;
+  for (int d = 0; d < L.world; ++d)
+    if (mask & (1u << d)) add_f32x16(acc, comb + (static_cast<size_t>(d) * L.t_max + t) * H + c0);
+  store_bf16x16(out + static_cast<size_t>(t) * H + c0, acc);
+}
+
+}  // namespace moe

@@ -164,7 +164,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
   uint8_t* smem = align_1024(smem_raw);
   G1Ctrl* ctl = reinterpret_cast<G1Ctrl*>(smem + G1_STAGES * G1_STAGE_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp == 0) build_tile_map(&ctl->map, p.counts, p.E_local, p.slots);
+  if (warp == 0) build_tile_map(&ctl->map, p.counts, p.E_local, p.slots, p.tiles_max);
   __syncthreads();
   const int n_units = clamp_tiles(ctl->map.tile_off[p.E_local], p.tiles_max) * G1_NT;
   if (static_cast<int>(blockIdx.x) >= n_units) return;  // uniform per CTA, before any TMEM use

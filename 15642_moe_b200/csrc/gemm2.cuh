@@ -62,7 +62,7 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
   uint8_t* smem = align_1024(smem_raw);
   G2Ctrl* ctl = reinterpret_cast<G2Ctrl*>(smem + G2_STAGES * G2_STAGE_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (warp == 0) build_tile_map(&ctl->map, p.counts, p.E_local, p.slots);
+  if (warp == 0) build_tile_map(&ctl->map, p.counts, p.E_local, p.slots, p.tiles_max);
   __syncthreads();
   if (blockIdx.x == 0)
     for (int e = threadIdx.x; e <= p.E_local; e += blockDim.x) p.dense_base[e] = ctl->map.dense_off[e];

@@ -7,16 +7,22 @@
  *   -> gemm2_weighted_kernel (tcgen05) -> combine_kernel
  * replacing the reference's route_dispatch / stage1 / stage2 / bf16_convert launches
  * (kernels/moe.cu:842-897).
+ *
+ * moe_ep_forward (expert parallel over W GPUs, ep.cuh): route -> ep_dispatch (peer stores)
+ *   -> barrier -> gather -> gemm1 -> gemm2 -> ep_combine_send (peer stores) -> memset(counts)
+ *   -> barrier -> ep_final_combine.
  */
 #include "moe_common.cuh"
 
 #include "route.cuh"
+#include "ep.cuh"
 #include "gemm1.cuh"
 #include "gemm2.cuh"
 #include "pack.cuh"
 #include "synth.cuh"
 #include "moe_b200.h"
 
+#include <cstring>
 #include <mutex>
 #include <string>
 
@@ -184,7 +190,7 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
                  const float* w13_scale, const void* w2_packed, const float* w2_scale,
                  const float* logits, const float* bias, float routed_scaling_factor,
                  int local_expert_offset, int T, int E_local, void* out_bf16, void* workspace,
-                 size_t workspace_bytes, void* stream, void* const* events) {
+                 size_t workspace_bytes, void* stream, void* const* events, bool out_f32 = false) {
   if (T < 0) return fail(MOE_ERR_INVALID, "hidden must be [T, 7168]");
   if (E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "W13_packed must be [E_local, ...] with 1 <= E_local <= 256");
   if (T == 0) return MOE_OK;
@@ -243,10 +249,112 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   const int g2_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G2_NT, 1, d->num_sms);
   gemm2_weighted_kernel<<<g2_grid, G2_THREADS, G2_SMEM, st>>>(g2);
   mark(4);
-  combine_kernel<<<T, COMBINE_THREADS, 0, st>>>(partial, token_nr, token_route, dense_base, T,
-                                                static_cast<__nv_bfloat16*>(out_bf16));
+  if (out_f32)
+    combine_kernel<float><<<T, COMBINE_THREADS, 0, st>>>(partial, token_nr, token_route, dense_base, T,
+                                                         E_local, static_cast<float*>(out_bf16));
+  else
+    combine_kernel<__nv_bfloat16><<<T, COMBINE_THREADS, 0, st>>>(partial, token_nr, token_route, dense_base,
+                                                                 T, E_local, static_cast<__nv_bfloat16*>(out_bf16));
   mark(5);
   return cuda_check(cudaGetLastError(), "moe_forward launch");
+}
+
+// ---- expert parallel -------------------------------------------------------------------
+
+struct EpCtx {
+  int rank = 0, world = 0, device = 0;
+  EpLayout L{};
+  uint8_t* local = nullptr;      // this rank's symmetric buffer (cudaMalloc)
+  EpPeers peers{};
+  bool opened[EP_MAX_RANKS] = {};  // peers[d] came from cudaIpcOpenMemHandle
+  bool connected = false;
+  unsigned epoch = 0;
+};
+
+int ep_check_shape(int world, int t_rank_max, int e_rank) {
+  if (world < 1 || world > EP_MAX_RANKS) return fail(MOE_ERR_INVALID, "moe_ep: world size must be 1..8");
+  if (t_rank_max < 1) return fail(MOE_ERR_INVALID, "moe_ep: t_rank_max must be >= 1");
+  if (static_cast<long long>(world) * t_rank_max > MAX_TOKENS)
+    return fail(MOE_ERR_INVALID, "moe_ep: world * t_rank_max must be at most 65536");
+  if (e_rank < 1 || static_cast<long long>(world) * e_rank > E_GLOBAL)
+    return fail(MOE_ERR_INVALID, "moe_ep: e_rank must be >= 1 with world * e_rank <= 256");
+  return MOE_OK;
+}
+
+int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, const void* w13_packed,
+                    const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                    const float* logits, const float* bias, float routed_scaling_factor, int T,
+                    void* out_bf16, void* workspace, size_t workspace_bytes, void* stream,
+                    void* const* events) {
+  if (c == nullptr || !c->connected) return fail(MOE_ERR_INVALID, "moe_ep_forward: context not connected");
+  if (T < 0 || T > c->L.t_max)
+    return fail(MOE_ERR_INVALID, "moe_ep_forward: T must be in [0, t_rank_max] (" + std::to_string(c->L.t_max) + ")");
+  if (!w13_packed || !w13_scale || !w2_packed || !w2_scale || !bias || !workspace ||
+      (T > 0 && (!hidden || !hidden_scale || !logits || !out_bf16)))
+    return fail(MOE_ERR_INVALID, "moe_ep_forward: null pointer argument");
+  const void* ptrs[] = {hidden, hidden_scale, w13_packed, w13_scale, w2_packed, w2_scale, logits, bias, out_bf16, workspace};
+  for (const void* q : ptrs)
+    if (!aligned16(q)) return fail(MOE_ERR_INVALID, "moe_ep_forward: every tensor must be 16-byte aligned");
+  const EpLayout& L = c->L;
+  const Workspace ws = make_workspace(L.r_cap, L.e_rank);
+  if (workspace_bytes < ws.total)
+    return fail(MOE_ERR_WORKSPACE, "workspace too small: need " + std::to_string(ws.total) + " bytes");
+  int dev = -1;
+  if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
+  if (dev != c->device) return fail(MOE_ERR_INVALID, "moe_ep_forward: current device differs from the context's");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  uint8_t* W = static_cast<uint8_t*>(workspace);
+  uint8_t* me = c->local;
+  int* topk_idx = reinterpret_cast<int*>(W + ws.topk_idx);
+  float* topk_w = reinterpret_cast<float*>(W + ws.topk_w);
+  int* dense_base = reinterpret_cast<int*>(W + ws.dense_base);
+  int* counts = ep_at<int>(me, L.counts);
+  uint8_t* a_tiled = W + ws.a_tiled;
+  float* a_scale = reinterpret_cast<float*>(W + ws.a_scale);
+  uint8_t* c_hi = W + ws.c_hi;
+  uint8_t* c_lo = W + ws.c_lo;
+  float* c_scale = reinterpret_cast<float*>(W + ws.c_scale);
+  float* partial = reinterpret_cast<float*>(W + ws.partial);
+  Gemm1Args g1{a_tiled, a_scale, static_cast<const uint8_t*>(w13_packed), w13_scale, counts, L.r_cap,
+               ws.tiles_max, L.e_rank, c_hi, c_lo, c_scale};
+  Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, counts, L.r_cap,
+               ws.tiles_max, L.e_rank, ep_at<float>(me, L.route_w), partial, dense_base};
+  const unsigned epoch = ++c->epoch;
+  auto mark = [&](int i) {
+    if (events != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
+  };
+  mark(0);
+  if (T > 0)
+    route_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, routed_scaling_factor, 0, 0, topk_idx, topk_w,
+                                              nullptr, nullptr, nullptr, nullptr, nullptr);
+  mark(1);
+  ep_dispatch_kernel<<<grid_for(static_cast<size_t>(T), 8, d->num_sms * 8), 256, 0, st>>>(
+      c->peers, L, c->rank, T, static_cast<const uint8_t*>(hidden), hidden_scale, topk_idx, topk_w);
+  mark(2);
+  ep_barrier_kernel<<<1, 32, 0, st>>>(c->peers, L.arrive, c->rank, L.world, epoch);
+  mark(3);
+  const size_t route_max = static_cast<size_t>(L.r_cap) * (L.e_rank < TOP_K ? L.e_rank : TOP_K);
+  gather_kernel<<<grid_for(route_max, 8, d->num_sms * 8), 256, 0, st>>>(
+      me + L.recv_rows, ep_at<float>(me, L.recv_scale), L.r_cap, counts, L.e_rank,
+      ep_at<int>(me, L.route_token), ws.tiles_max, a_tiled, a_scale);
+  mark(4);
+  gemm1_swiglu_kernel<<<grid_for(static_cast<size_t>(ws.tiles_max) * G1_NT, 1, d->num_sms), G1_THREADS, G1_SMEM, st>>>(g1);
+  mark(5);
+  gemm2_weighted_kernel<<<grid_for(static_cast<size_t>(ws.tiles_max) * G2_NT, 1, d->num_sms), G2_THREADS, G2_SMEM, st>>>(g2);
+  mark(6);
+  ep_combine_send_kernel<<<grid_for(static_cast<size_t>(L.r_cap), 1, d->num_sms * 4), COMBINE_THREADS, 0, st>>>(
+      c->peers, L, c->rank, partial, dense_base);
+  if (int rc = cuda_check(cudaMemsetAsync(counts, 0, sizeof(int) * L.e_rank, st), "memset counts")) return rc;
+  mark(7);
+  ep_barrier_kernel<<<1, 32, 0, st>>>(c->peers, L.done, c->rank, L.world, epoch);
+  mark(8);
+  if (T > 0)
+    ep_final_combine_kernel<<<T, COMBINE_THREADS, 0, st>>>(me, L, T, topk_idx, static_cast<__nv_bfloat16*>(out_bf16));
+  mark(9);
+  return cuda_check(cudaGetLastError(), "moe_ep_forward launch");
 }
 
 }  // namespace
@@ -261,6 +369,16 @@ int moe_forward(const void* hidden, const float* hidden_scale, const void* w13_p
   return forward_impl(hidden, hidden_scale, w13_packed, w13_scale, w2_packed, w2_scale, logits, bias,
                       routed_scaling_factor, local_expert_offset, T, E_local, out_bf16, workspace,
                       workspace_bytes, stream, nullptr);
+}
+
+int moe_forward_f32(const void* hidden, const float* hidden_scale, const void* w13_packed,
+                    const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                    const float* logits, const float* bias, float routed_scaling_factor,
+                    int local_expert_offset, int T, int E_local, float* out_f32, void* workspace,
+                    size_t workspace_bytes, void* stream) {
+  return forward_impl(hidden, hidden_scale, w13_packed, w13_scale, w2_packed, w2_scale, logits, bias,
+                      routed_scaling_factor, local_expert_offset, T, E_local, out_f32, workspace,
+                      workspace_bytes, stream, nullptr, true);
 }
 
 int moe_forward_noalloc(const void* hidden, const float* hidden_scale, const void* w13_packed,
@@ -357,6 +475,117 @@ int moe_synth_w2(const float* table, uint64_t seed, int e0, int E, float stddev,
   synth_weight_kernel<<<blocks, 256, 0, static_cast<cudaStream_t>(stream)>>>(
       table, seed, SYN_W2, e0, H, I, stddev, static_cast<uint8_t*>(w2), w2_scale);
   return cuda_check(cudaGetLastError(), "synth_w2 launch");
+}
+
+
+size_t moe_ep_symmetric_bytes(int world, int t_rank_max, int e_rank) {
+  if (ep_check_shape(world, t_rank_max, e_rank) != MOE_OK) return 0;
+  return make_ep_layout(world, t_rank_max, e_rank).total;
+}
+
+size_t moe_ep_workspace_bytes(int world, int t_rank_max, int e_rank) {
+  if (ep_check_shape(world, t_rank_max, e_rank) != MOE_OK) return 0;
+  return make_workspace(world * t_rank_max, e_rank).total;
+}
+
+int moe_ep_create(int rank, int world, int t_rank_max, int e_rank, void** ctx, void* ipc_handle) {
+  if (ctx == nullptr || ipc_handle == nullptr) return fail(MOE_ERR_INVALID, "moe_ep_create: null pointer argument");
+  *ctx = nullptr;
+  if (int rc = ep_check_shape(world, t_rank_max, e_rank)) return rc;
+  if (rank < 0 || rank >= world) return fail(MOE_ERR_INVALID, "moe_ep_create: rank must be in [0, world)");
+  static_assert(sizeof(cudaIpcMemHandle_t) == MOE_EP_HANDLE_BYTES, "IPC handle size");
+  EpCtx* c = new EpCtx();
+  c->rank = rank;
+  c->world = world;
+  c->L = make_ep_layout(world, t_rank_max, e_rank);
+  int rc = cuda_check(cudaGetDevice(&c->device), "cudaGetDevice");
+  if (!rc) rc = cuda_check(cudaMalloc(&c->local, c->L.total), "cudaMalloc(symmetric buffer)");
+  if (!rc) rc = cuda_check(cudaMemset(c->local, 0, c->L.total), "cudaMemset(symmetric buffer)");
+  cudaIpcMemHandle_t h{};
+  if (!rc) rc = cuda_check(cudaIpcGetMemHandle(&h, c->local), "cudaIpcGetMemHandle");
+  if (rc) {
+    if (c->local) cudaFree(c->local);
+    delete c;
+    return rc;
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ctx = c;
+  return MOE_OK;
+}
+
+int moe_ep_connect(void* ctx, const void* handles) {
+  EpCtx* c = static_cast<EpCtx*>(ctx);
+  if (c == nullptr || handles == nullptr) return fail(MOE_ERR_INVALID, "moe_ep_connect: null pointer argument");
+  if (c->connected) return fail(MOE_ERR_INVALID, "moe_ep_connect: already connected");
+  const uint8_t* hb = static_cast<const uint8_t*>(handles);
+  for (int d = 0; d < c->world; ++d) {
+    if (d == c->rank) {
+      c->peers.base[d] = c->local;
+      continue;
+    }
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, hb + static_cast<size_t>(d) * MOE_EP_HANDLE_BYTES, sizeof(h));
+    void* p = nullptr;
+    if (int rc = cuda_check(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess), "cudaIpcOpenMemHandle")) {
+      for (int k = 0; k < d; ++k)
+        if (c->opened[k]) {
+          cudaIpcCloseMemHandle(c->peers.base[k]);
+          c->opened[k] = false;
+        }
+      return rc;
+    }
+    c->peers.base[d] = static_cast<uint8_t*>(p);
+    c->opened[d] = true;
+  }
+  c->connected = true;
+  return MOE_OK;
+}
+
+int moe_ep_destroy(void* ctx) {
+  EpCtx* c = static_cast<EpCtx*>(ctx);
+  if (c == nullptr) return MOE_OK;
+  int rc = MOE_OK;
+  for (int d = 0; d < EP_MAX_RANKS; ++d)
+    if (c->opened[d]) {
+      int r = cuda_check(cudaIpcCloseMemHandle(c->peers.base[d]), "cudaIpcCloseMemHandle");
+      if (!rc) rc = r;
+    }
+  if (c->local) {
+    int r = cuda_check(cudaFree(c->local), "cudaFree(symmetric buffer)");
+    if (!rc) rc = r;
+  }
+  delete c;
+  return rc;
+}
+
+int moe_ep_forward(void* ctx, const void* hidden, const float* hidden_scale, const void* w13_packed,
+                   const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                   const float* logits, const float* bias, float routed_scaling_factor, int T,
+                   void* out_bf16, void* workspace, size_t workspace_bytes, void* stream) {
+  return ep_forward_impl(static_cast<EpCtx*>(ctx), hidden, hidden_scale, w13_packed, w13_scale, w2_packed,
+                         w2_scale, logits, bias, routed_scaling_factor, T, out_bf16, workspace,
+                         workspace_bytes, stream, nullptr);
+}
+
+int moe_ep_forward_profiled(void* ctx, const void* hidden, const float* hidden_scale,
+                            const void* w13_packed, const float* w13_scale, const void* w2_packed,
+                            const float* w2_scale, const float* logits, const float* bias,
+                            float routed_scaling_factor, int T, void* out_bf16, void* workspace,
+                            size_t workspace_bytes, void* stream, void* const* events) {
+  if (events == nullptr) return fail(MOE_ERR_INVALID, "moe_ep_forward_profiled: events must not be null");
+  return ep_forward_impl(static_cast<EpCtx*>(ctx), hidden, hidden_scale, w13_packed, w13_scale, w2_packed,
+                         w2_scale, logits, bias, routed_scaling_factor, T, out_bf16, workspace,
+                         workspace_bytes, stream, events);
+}
+
+int moe_ep_info(void* ctx, int* out4) {
+  EpCtx* c = static_cast<EpCtx*>(ctx);
+  if (c == nullptr || out4 == nullptr) return fail(MOE_ERR_INVALID, "moe_ep_info: null pointer argument");
+  out4[0] = c->rank;
+  out4[1] = c->world;
+  out4[2] = c->L.t_max;
+  out4[3] = c->L.e_rank;
+  return MOE_OK;
 }
 
 }  // extern "C"

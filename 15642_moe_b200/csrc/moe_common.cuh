@@ -39,6 +39,7 @@ constexpr int ST_TIMEOUT_PRODUCER = 1;
 constexpr int ST_TIMEOUT_MMA = 2;
 constexpr int ST_TIMEOUT_EPILOGUE = 4;
 constexpr int ST_BAD_INDEX = 8;
+constexpr int ST_EP_TIMEOUT = 16;        // an expert-parallel barrier gave up waiting for a peer
 
 // A bounded wait gives up after this long and reports ST_TIMEOUT_*.
 constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;  // 2 s
@@ -60,6 +61,16 @@ __device__ __forceinline__ unsigned long long globaltimer() {
 }
 
 __device__ __forceinline__ void report_status(int bits) { atomicOr(&g_status, bits); }
+
+// System-scope flag accesses for the expert-parallel barriers (peer memory over NVLink).
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
 
 // Routing metadata is produced on the device; a consumer never trusts it for addressing.
 __device__ __forceinline__ int clamp_tiles(int n, int tiles_max) {
@@ -395,9 +406,11 @@ struct TileMap {
 };
 
 // Built by one full warp; the caller synchronises before use. A count outside [0, cap] is
-// reported and clamped, so a corrupted count can never address past the workspace.
+// reported and clamped; counts whose totals exceed what the workspace was sized for
+// (cap * min(8, E_local) routes, tiles_max tiles) are reported and replaced by an empty map,
+// so corrupted counts can never address past the workspace.
 __device__ __forceinline__ void build_tile_map(TileMap* tm, const int* __restrict__ counts,
-                                               int E_local, int cap) {
+                                               int E_local, int cap, int tiles_max) {
   const int lane = threadIdx.x & 31;
   int c[8], tiles = 0, rows = 0;
 #pragma unroll
@@ -423,6 +436,15 @@ __device__ __forceinline__ void build_tile_map(TileMap* tm, const int* __restric
     }
   }
   int t = t_incl - tiles, r = r_incl - rows;
+  const int all_tiles = __shfl_sync(0xffffffffu, t_incl, 31);
+  const int all_rows = __shfl_sync(0xffffffffu, r_incl, 31);
+  const long long rows_max = static_cast<long long>(cap) * (E_local < TOP_K ? E_local : TOP_K);
+  if (all_tiles > tiles_max || all_rows > rows_max) {
+    if (lane == 0) report_status(ST_BAD_INDEX);
+    t = r = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) c[i] = 0;
+  }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
     const int e = lane * 8 + i;

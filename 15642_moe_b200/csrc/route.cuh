@@ -194,7 +194,7 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__
                                                      int tiles_max, uint8_t* __restrict__ a_tiled,
                                                      float* __restrict__ a_scale) {
   __shared__ TileMap map;
-  if (threadIdx.x < 32) build_tile_map(&map, counts, E_local, T);
+  if (threadIdx.x < 32) build_tile_map(&map, counts, E_local, T, tiles_max);
   __syncthreads();
   const int routes = map.dense_off[E_local];
   const int lane = threadIdx.x & 31;
@@ -233,28 +233,27 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// One CTA per token: out[t] = bf16( sum over its local routes, ascending expert order,
-// of the weighted expert outputs ), starting from +0 like the reference's zero tensor.
-// dense_base[le] = number of local routes of experts < le (written by the GEMM2 kernel), so
-// route (le, slot) of a token is row dense_base[le] + slot of `partial`.
-__global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(const float* __restrict__ partial,
-                                                                  const int* __restrict__ token_nr,
-                                                                  const int* __restrict__ token_route,
-                                                                  const int* __restrict__ dense_base,
-                                                                  int T,
-                                                                  __nv_bfloat16* __restrict__ out) {
-  const int t = blockIdx.x;
-  if (t >= T) return;
-  const int n = token_nr[t];
-  const int c0 = threadIdx.x * 16;
-  float acc[16];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+// Adds a token's weighted expert outputs to acc[16] (columns c0..c0+15): `routes` holds n
+// entries (le << 16) | slot in ascending le, and route (le, slot) is row dense_base[le] + slot
+// of `partial` (dense_base written by the GEMM2 kernel, entry [E_local] = all routes). Each
+// entry is checked against the expert's row range before it addresses anything.
+__device__ __forceinline__ void add_routes(float (&acc)[16], const float* __restrict__ partial,
+                                           const int* __restrict__ routes, int n,
+                                           const int* __restrict__ dense_base, int E_local, int c0) {
 #pragma unroll
   for (int k = 0; k < TOP_K; ++k) {
     if (k < n) {
-      const int packed = token_route[static_cast<size_t>(t) * TOP_K + k];
-      const int row = dense_base[packed >> 16] + (packed & 0xFFFF);
+      const unsigned packed = static_cast<unsigned>(routes[k]);
+      const int le = static_cast<int>(packed >> 16), slot = static_cast<int>(packed & 0xFFFFu);
+      if (le >= E_local) {
+        report_status(ST_BAD_INDEX);
+        continue;
+      }
+      const int row = dense_base[le] + slot;
+      if (row >= dense_base[le + 1]) {
+        report_status(ST_BAD_INDEX);
+        continue;
+      }
       const float4* src = reinterpret_cast<const float4*>(partial + static_cast<size_t>(row) * H + c0);
       float4 p[4];
 #pragma unroll
@@ -268,6 +267,10 @@ __global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(const float* _
       }
     }
   }
+}
+
+// Rounds acc[16] once to bf16 and stores the 32 bytes at dst.
+__device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&acc)[16]) {
   uint4 o0, o1;
   o0.x = pack_bf16x2(acc[0], acc[1]);
   o0.y = pack_bf16x2(acc[2], acc[3]);
@@ -277,9 +280,38 @@ __global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(const float* _
   o1.y = pack_bf16x2(acc[10], acc[11]);
   o1.z = pack_bf16x2(acc[12], acc[13]);
   o1.w = pack_bf16x2(acc[14], acc[15]);
-  uint4* dst = reinterpret_cast<uint4*>(out + static_cast<size_t>(t) * H + c0);
-  dst[0] = o0;
-  dst[1] = o1;
+  uint4* d = reinterpret_cast<uint4*>(dst);
+  d[0] = o0;
+  d[1] = o1;
+}
+
+// Stores acc[16] unrounded (64 bytes at dst).
+__device__ __forceinline__ void store_f32x16(float* dst, const float (&acc)[16]) {
+  float4* d = reinterpret_cast<float4*>(dst);
+#pragma unroll
+  for (int j = 0; j < 4; ++j) d[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+}
+
+// One CTA per token: out[t] = sum over its local routes, ascending expert order, of the
+// weighted expert outputs, starting from +0 like the reference's zero tensor; rounded once to
+// bf16 (OutT = __nv_bfloat16, moe_ref.py:136) or left in fp32 (OutT = float).
+template <typename OutT>
+__global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(const float* __restrict__ partial,
+                                                                  const int* __restrict__ token_nr,
+                                                                  const int* __restrict__ token_route,
+                                                                  const int* __restrict__ dense_base,
+                                                                  int T, int E_local, OutT* __restrict__ out) {
+  const int t = blockIdx.x;
+  if (t >= T) return;
+  const int c0 = threadIdx.x * 16;
+  float acc[16];
+#pragma unroll
+  for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
+  add_routes(acc, partial, token_route + static_cast<size_t>(t) * TOP_K, token_nr[t], dense_base, E_local, c0);
+  if constexpr (sizeof(OutT) == 2)
+    store_bf16x16(out + static_cast<size_t>(t) * H + c0, acc);
+  else
+    store_f32x16(out + static_cast<size_t>(t) * H + c0, acc);
 }
 
 }  // namespace moe

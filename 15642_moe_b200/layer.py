@@ -72,11 +72,12 @@ def workspace_bytes(T: int, E_local: int) -> int:
 
 def moe_forward(hidden, hidden_scale, W13_packed, W13_scale, W2_packed, W2_scale, logits, bias,
                 rsf: float, local_offset: int, out: torch.Tensor | None = None,
-                workspace: torch.Tensor | None = None) -> torch.Tensor:
+                workspace: torch.Tensor | None = None, *, fp32_out: bool = False) -> torch.Tensor:
     """bf16 [T, 7168] MoE output; argument order of kernels/moe.cu:744-754.
 
     ``out`` and ``workspace`` may be passed to reuse buffers (e.g. inside a CUDA graph);
     otherwise they come from the PyTorch caching allocator like the reference's scratch.
+    ``fp32_out=True`` returns the fp32 sum before the final bf16 rounding (moe_forward_f32).
     """
     # Shape / dtype / contiguity checks with the reference's messages (kernels/moe.cu:759-817).
     _check(hidden.dim() == 2, "hidden must be [T, 7168]")
@@ -113,18 +114,20 @@ def moe_forward(hidden, hidden_scale, W13_packed, W13_scale, W2_packed, W2_scale
     _check(all(t.device == dev for t in (hidden_scale, W13_packed, W13_scale, W2_packed, W2_scale,
                                           logits, bias)), "all tensors must be on one device")
     lib = _native.cuda_lib()
+    out_dtype = torch.float32 if fp32_out else torch.bfloat16
     if out is None:
-        out = torch.empty((T, H), dtype=torch.bfloat16, device=dev)
-    _check(out.dtype == torch.bfloat16 and tuple(out.shape) == (T, H) and out.is_contiguous(),
-           "out must be a contiguous bf16 [T, 7168] tensor")
+        out = torch.empty((T, H), dtype=out_dtype, device=dev)
+    _check(out.dtype == out_dtype and tuple(out.shape) == (T, H) and out.is_contiguous(),
+           f"out must be a contiguous {'fp32' if fp32_out else 'bf16'} [T, 7168] tensor")
     nbytes = int(lib.moe_forward_workspace_bytes(T, E_local)) if T > 0 else 0
     if workspace is None:
         workspace = torch.empty((max(nbytes, 1),), dtype=torch.uint8, device=dev)
     _check(workspace.numel() >= nbytes, f"workspace must hold {nbytes} bytes")
     if T == 0:
         return out
+    fn = lib.moe_forward_f32 if fp32_out else lib.moe_forward
     with torch.cuda.device(dev):
-        _native.check(lib.moe_forward(
+        _native.check(fn(
             hidden.data_ptr(), hidden_scale.data_ptr(), W13_packed.data_ptr(), W13_scale.data_ptr(),
             W2_packed.data_ptr(), W2_scale.data_ptr(), logits.data_ptr(), bias.data_ptr(),
             float(rsf), int(local_offset), T, E_local, out.data_ptr(), workspace.data_ptr(),

@@ -9,9 +9,11 @@ full moe_forward: route -> gather -> GEMM1+SwiGLU -> GEMM2 -> combine. The
 1.41 GB of FP8 expert weights exceed the 126 MB L2, so no flush is needed between steps.
 The decode case (configuration 1, T=64) is reported alongside as microseconds per layer.
 
-Under torchrun (N > 1) every rank runs the same step on its own 32-expert slice of the
-256-expert layer (local_expert_offset = 32 * rank), without a data-path collective; the
-reported value is all ranks' tokens / max-over-ranks device time ("weak" scaling).
+Under torchrun (N > 1) the layer runs expert-parallel (15642_moe_b200/ep.py): rank r owns
+experts 32r..32r+31, the 4096 tokens are split over the ranks, token rows travel to their
+experts' owners and partial results back as peer stores over NVLink issued by the kernels.
+Per-GPU work stays that of configuration 2 ("weak" scaling); the value counts each token once
+per 32-expert slice it passes through, over the max-over-ranks device time.
 
 --impl reference times the CPU restatement of reference/moe_ref.py (oracle/) on the host
 cores, on the same configuration (rank 0 only).
@@ -224,9 +226,11 @@ def load_traffic(workload: str) -> dict | None:
         return json.load(f).get(workload)
 
 
-def e2e_run(pkg, inp, device, steps: int, warmup: int) -> dict:
-    """Public API (pkg.run) per step: H2D of the step's activations from pinned host memory,
-    the forward with resident weights, D2H of the bf16 result."""
+def e2e_run(pkg, inp, device, steps: int, warmup: int, call=None) -> dict:
+    """Public API (pkg.run, or `call` with the same keywords) per step: H2D of the step's
+    activations from pinned host memory, the forward with resident weights, D2H of the bf16
+    result."""
+    call = pkg.run if call is None else call
     host = {k: inp[k].cpu().pin_memory() for k in ("hidden_states", "hidden_states_scale", "routing_logits")}
     dev = {k: torch.empty_like(inp[k]) for k in host}
     out_host = torch.empty((inp["hidden_states"].shape[0], 7168), dtype=torch.bfloat16).pin_memory()
@@ -236,7 +240,7 @@ def e2e_run(pkg, inp, device, steps: int, warmup: int) -> dict:
         for k in host:
             dev[k].copy_(host[k], non_blocking=True)
         kw.update(dev)
-        out = pkg.run(**kw)
+        out = call(**kw)
         out_host.copy_(out, non_blocking=True)
 
     for _ in range(warmup):
@@ -373,6 +377,143 @@ def bench_ours(args, rank, world, local_rank, dist):
     return line
 
 
+def ep_routing_stats(pkg, inp, rank: int, e_rank: int) -> dict:
+    """Routes and active experts that `rank` receives (picks of its experts over all tokens)."""
+    idx, _ = pkg.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"])
+    idx = idx.cpu().numpy()
+    lo = rank * e_rank
+    local = (idx >= lo) & (idx < lo + e_rank)
+    counts = np.bincount((idx[local] - lo).ravel(), minlength=e_rank)
+    return dict(routes=int(local.sum()), active=int((counts > 0).sum()),
+                max_per_expert=int(counts.max()), tiles=int(((counts + 127) // 128).sum()))
+
+
+def bench_ep(args, rank, world, local_rank, dist):
+    """Expert-parallel layer over `world` GPUs (weak scaling of configuration 2's per-GPU work).
+
+    Every rank owns 32 experts (rank r: experts 32r..32r+31, so N ranks hold 32N of the 256
+    and N = 8 is the full layer); the T = 4096 tokens of configuration 2 are split evenly over
+    the ranks. Each rank therefore streams the weights of 32 experts and receives, in
+    expectation, the routes of 4096 token-slices, as the one GPU of configuration 2 does.
+    `value` counts each token once per 32-expert slice it passes through (4096 * N per step),
+    the unit configuration 2 is measured in at N = 1; `layer_tokens_per_s` is 4096 per step.
+    """
+    pkg = importlib.import_module("15642_moe_b200")
+    epm = importlib.import_module("15642_moe_b200.ep")
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    peaks = load_peaks()
+    e_rank, T_global = 32, pkg.CONFIGS[2].T
+    cfg = pkg.CONFIGS[2].with_(local_expert_offset=e_rank * rank)
+    inp = pkg.make_inputs(cfg, device)
+    rs = ep_routing_stats(pkg, inp, rank, e_rank)
+    lo, hi = epm.token_range(T_global, world, rank)
+    mine = dict(inp)
+    mine["hidden_states"] = inp["hidden_states"][lo:hi].contiguous()
+    mine["hidden_states_scale"] = inp["hidden_states_scale"][:, lo:hi].contiguous()
+    mine["routing_logits"] = inp["routing_logits"][lo:hi].contiguous()
+    T_r = hi - lo
+    w13p, w2p = pkg.pack_w13(inp["gemm1_weights"]), pkg.pack_w2(inp["gemm2_weights"])
+    k = dict(hidden=mine["hidden_states"], hs=mine["hidden_states_scale"].float().contiguous(),
+             s13=inp["gemm1_weights_scale"].float().contiguous(), s2=inp["gemm2_weights_scale"].float().contiguous(),
+             lg=mine["routing_logits"].float().contiguous(), b=inp["routing_bias"].float().reshape(-1).contiguous())
+    out = torch.empty((T_r, 7168), dtype=torch.bfloat16, device=device)
+    ctx = epm.ExpertParallel(t_rank_max=T_r, e_rank=e_rank, device=device)
+
+    def step(events=None):
+        ctx.forward(k["hidden"], k["hs"], w13p, k["s13"], w2p, k["s2"], k["lg"], k["b"],
+                    float(cfg.routed_scaling_factor), out=out, events=events)
+
+    try:
+        for _ in range(args.warmup):
+            step()
+        torch.cuda.synchronize()
+        sampler = ClockSampler(local_rank)
+        sampler.start()
+        t_end = time.time() + args.burn_in
+        n_burn = torch.zeros(1, device=device)
+        while True:                   # every rank runs the same number of steps
+            go = torch.tensor([1.0 if time.time() < t_end else 0.0], device=device)
+            dist.all_reduce(go, op=dist.ReduceOp.MIN)
+            if go.item() == 0.0:
+                break
+            for _ in range(20):
+                step()
+            torch.cuda.synchronize()
+            n_burn += 20
+        dist.barrier()
+        torch.cuda.synchronize()
+        ms = time_steps(step, args.steps)
+        t = torch.tensor([ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+        clocks = sampler.stop()
+        status = pkg.device_status(reset=True)
+
+        reps = min(args.steps, 30)
+        names = epm.EP_EVENTS
+        evs = [[torch.cuda.Event(enable_timing=True) for _ in range(len(names) + 1)] for _ in range(reps)]
+        for row in evs:
+            for ev in row:
+                ev.record()
+        torch.cuda.synchronize()
+        dist.barrier()
+        for r in range(reps):
+            step(evs[r])
+        torch.cuda.synchronize()
+        stages = {n: statistics.mean(evs[r][i].elapsed_time(evs[r][i + 1]) for r in range(reps))
+                  for i, n in enumerate(names)}
+        work = kernel_work(rs, T_r)
+        roof = roofline(stages, work, peaks, load_traffic("prefill_t4096") if rank == 0 else None)
+
+        kw = {kk: v for kk, v in mine.items() if kk != "local_expert_offset"}
+        e2e = e2e_run(pkg, kw, device, args.steps, args.warmup, call=ctx.run)
+        t = torch.tensor([e2e["ms_per_step"]], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e["ms_per_step"] = float(t.item())
+        routes_all = torch.tensor([rs["routes"]], device=device, dtype=torch.float64)
+        dist.all_reduce(routes_all)
+    finally:
+        ctx.close()
+    if rank != 0:
+        return None
+    slices = T_global * world
+    return {
+        "metric": METRIC,
+        "value": round(slices * args.steps / (ms * 1e-3), 1),
+        "unit": "tokens/s",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms / args.steps, 5),
+        "higher_is_better": True,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "e4m3 (fp32 accumulate)",
+        "data": "synthetic: seeded N(0,1) logits/hidden, N(0,0.1) bias, N(0,0.02) weights, "
+                "e4m3 with amax/448 128-block scales",
+        "config": {"workload": "ep_weak_config2_t4096", "T_global": T_global, "T_per_rank": T_r,
+                   "experts_per_rank": e_rank, "experts_instantiated": e_rank * world,
+                   "experts_total": 256, "routed_scaling_factor": cfg.routed_scaling_factor,
+                   "seed": cfg.seed, "parallelism": f"ep{world}: dispatch/combine as peer stores over NVLink",
+                   "token_count": "each token counted once per 32-expert slice it passes through "
+                                  f"({T_global} x {world} per step); N=8 is the full 256-expert layer",
+                   "routes_all_ranks": int(routes_all.item()), "routes_rank0": rs["routes"],
+                   "active_experts_rank0": rs["active"],
+                   "l2": "inputs larger than L2 (1.41 GB FP8 expert weights per rank per step)"},
+        "layer_tokens_per_s": round(T_global * args.steps / (ms * 1e-3), 1),
+        "roofline": roof,
+        "stage_us_rank0": {kk: round(v * 1e3, 2) for kk, v in stages.items()},
+        "e2e": {"value": round(slices / (e2e["ms_per_step"] * 1e-3), 1), "unit": "tokens/s",
+                "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
+                "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
+                "ms_per_step": round(e2e["ms_per_step"], 4), "per": "rank 0 (max over ranks)"},
+        "gpu_launches": 9 * args.steps,
+        "clocks": clocks,
+        "device_status": status,
+    }
+
+
 def bench_reference(args, rank):
     """CPU restatement of the reference (oracle/) on the host cores, same config / metric."""
     if rank != 0:
@@ -444,7 +585,7 @@ def main():
                                  device_id=torch.device("cuda", local_rank))
         dist = tdist
     try:
-        line = bench_ours(args, rank, world, local_rank, dist)
+        line = (bench_ours if world == 1 else bench_ep)(args, rank, world, local_rank, dist)
         if line is not None:
             print(json.dumps(line), flush=True)
     finally:

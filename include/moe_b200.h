@@ -40,7 +40,8 @@ extern "C" {
 const char* moe_last_error(void);
 
 /* Device status word written by kernels (bit 1/2/4: a bounded wait of the producer / MMA /
- * epilogue role timed out; bit 8: inconsistent routing metadata). Synchronises the device.
+ * epilogue role timed out; bit 8: inconsistent routing metadata; bit 16: an expert-parallel
+ * barrier timed out waiting for a peer rank). Synchronises the device.
  * When reset != 0 the word is cleared after reading. No reference counterpart: the
  * reference never checks kernel-side failures. */
 int moe_get_status(int* status, int reset);
@@ -105,6 +106,18 @@ int moe_forward_noalloc(const void* hidden, const float* hidden_scale, const voi
                         const float* logits, const float* bias, float routed_scaling_factor,
                         int local_expert_offset, int T, int E_local, void* out_bf16, void* stream);
 
+/* moe_forward with the output left in fp32: out_f32 fp32 [T, 7168] receives the per-token sum
+ * of the weighted expert outputs before the final bf16 rounding of reference/moe_ref.py:136
+ * (moe_forward's result is exactly its bf16 rounding). For callers that add further fp32 terms
+ * (another expert slice, a shared expert, the residual) and round once at the end. No
+ * reference counterpart: the reference keeps this fp32 buffer internal (kernels/moe.cu:
+ * 828-897). Other arguments as moe_forward. */
+int moe_forward_f32(const void* hidden, const float* hidden_scale, const void* w13_packed,
+                    const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                    const float* logits, const float* bias, float routed_scaling_factor,
+                    int local_expert_offset, int T, int E_local, float* out_f32, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
 /* moe_forward that also records events[0..5] (cudaEvent_t) on `stream`: before the first
  * launch and after each of its five kernels (route, gather, gemm1, gemm2, combine), for
  * per-kernel timing. No reference counterpart (instrumentation only). */
@@ -140,6 +153,69 @@ int moe_synth_w13(const float* table, uint64_t seed, int e0, int E, float stddev
                   float* w13_scale, void* stream);
 int moe_synth_w2(const float* table, uint64_t seed, int e0, int E, float stddev, void* w2,
                  float* w2_scale, void* stream);
+
+/* ---- Expert-parallel layer over W GPUs of one node (W <= 8), one process per GPU ----
+ *
+ * Rank r owns global experts [r * e_rank, (r + 1) * e_rank) (world * e_rank <= 256; picks of
+ * experts beyond world * e_rank are dropped like non-local experts in reference/moe_ref.py:
+ * 115-116) and holds its own tokens. moe_ep_forward returns, for the rank's own tokens, the
+ * layer output over all owned experts of all ranks: per owner rank the fp32 sum of its routes
+ * in ascending expert order (moe_forward_f32's result for that rank's experts), then the fp32
+ * sum of those partials in ascending rank order, rounded once to bf16. Token rows and fp32
+ * partial results move between the
+ * GPUs as peer stores issued by the kernels (CUDA IPC mappings over NVLink); the only host
+ * collective is the one-time exchange of the IPC handles (moe_ep_connect). Synchronisation
+ * between ranks is by epoch flags with bounded waits (2 s; status bit 16 on timeout).
+ *
+ * No reference counterpart: the reference's moe_forward (kernels/moe.cu:744-900) runs on one
+ * GPU over 32 local experts. Its semantics per rank are those of moe_forward_f32 with
+ * local_expert_offset = r * e_rank, summed over ranks and rounded once.
+ *
+ * Protocol: every rank calls moe_ep_create (allocates its symmetric buffer, returns its IPC
+ * handle), the handles are all-gathered in rank order, every rank calls moe_ep_connect, then
+ * a host barrier; then all ranks call moe_ep_forward the same number of times, in the same
+ * order (T may differ per rank and may be 0); teardown is a device synchronise and a host
+ * barrier on every rank followed by moe_ep_destroy. */
+#define MOE_EP_HANDLE_BYTES 64
+
+/* Bytes of the per-rank symmetric buffer and of moe_ep_forward's workspace; 0 for an invalid
+ * shape (world 1..8, t_rank_max >= 1, world * t_rank_max <= 65536, world * e_rank <= 256). */
+size_t moe_ep_symmetric_bytes(int world, int t_rank_max, int e_rank);
+size_t moe_ep_workspace_bytes(int world, int t_rank_max, int e_rank);
+
+/* Creates rank `rank`'s context on the current device: allocates and zeroes the symmetric
+ * buffer (synchronous) and writes its CUDA IPC handle (MOE_EP_HANDLE_BYTES) to ipc_handle. */
+int moe_ep_create(int rank, int world, int t_rank_max, int e_rank, void** ctx, void* ipc_handle);
+
+/* Maps the peers' buffers: handles = world * MOE_EP_HANDLE_BYTES, rank order. */
+int moe_ep_connect(void* ctx, const void* handles);
+
+/* Unmaps the peers and frees the buffer. Call only after every rank has finished its last
+ * moe_ep_forward (device synchronise + host barrier). */
+int moe_ep_destroy(void* ctx);
+
+/* rank, world, t_rank_max, e_rank of a context. */
+int moe_ep_info(void* ctx, int* out4);
+
+/* One expert-parallel layer forward for this rank's T <= t_rank_max tokens:
+ *   hidden e4m3 [T, 7168], hidden_scale fp32 [56, T], logits fp32 [T, 256], bias fp32 [256],
+ *   w13_packed / w2_packed: this rank's e_rank experts (moe_pack_w13 / moe_pack_w2),
+ *   w13_scale fp32 [e_rank, 32, 56], w2_scale fp32 [e_rank, 56, 16],
+ *   out_bf16 bf16 [T, 7168]; workspace of moe_ep_workspace_bytes(world, t_rank_max, e_rank).
+ * Asynchronous on `stream`; the call itself never waits for other ranks. */
+int moe_ep_forward(void* ctx, const void* hidden, const float* hidden_scale, const void* w13_packed,
+                   const float* w13_scale, const void* w2_packed, const float* w2_scale,
+                   const float* logits, const float* bias, float routed_scaling_factor, int T,
+                   void* out_bf16, void* workspace, size_t workspace_bytes, void* stream);
+
+/* moe_ep_forward recording events[0..9] on `stream`: before the first launch and after route,
+ * dispatch, arrival barrier, gather, gemm1, gemm2, combine-send (+ counts reset), completion
+ * barrier and final combine. Instrumentation only. */
+int moe_ep_forward_profiled(void* ctx, const void* hidden, const float* hidden_scale,
+                            const void* w13_packed, const float* w13_scale, const void* w2_packed,
+                            const float* w2_scale, const float* logits, const float* bias,
+                            float routed_scaling_factor, int T, void* out_bf16, void* workspace,
+                            size_t workspace_bytes, void* stream, void* const* events);
 
 #ifdef __cplusplus
 }

@@ -136,12 +136,16 @@ def expert_rows(topk_idx: np.ndarray, ge: int) -> np.ndarray:
 
 def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale, gemm1_weights,
                 gemm1_weights_scale, gemm2_weights, gemm2_weights_scale, local_expert_offset,
-                routed_scaling_factor, experts=None, return_fp32=False, return_routing=False):
+                routed_scaling_factor, experts=None, return_fp32=False, return_routing=False,
+                accumulate=None):
     """bf16 bits [T, 7168] of reference/moe_ref.py:run on numpy inputs.
 
     ``hidden_states``/``gemm*_weights`` are e4m3 codes (uint8); ``routing_bias`` float32.
     ``experts`` optionally restricts the computation to a subset of local expert indices
     (the output then holds only their contributions - used for bounded CPU timing samples).
+    ``accumulate`` (fp32 [T, 7168]) replaces the zero tensor of moe_ref.py:110, so calls over
+    consecutive expert slices chain into one layer of more experts with a single final rounding
+    (the semantics moe_ref.py would have with all those experts local).
     """
     logits = np.asarray(routing_logits, np.float32)
     T = logits.shape[0]
@@ -153,7 +157,7 @@ def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale
     assert gemm2_weights.shape == (E_local, H, I)
     topk_idx, topk_w = route(logits, routing_bias, routed_scaling_factor)
     A = dequant_hidden(hidden_states, hidden_states_scale)
-    out = np.zeros((T, H), np.float32)                       # moe_ref.py:110
+    out = np.zeros((T, H), np.float32) if accumulate is None else np.array(accumulate, np.float32)  # :110
     work = []
     for le in (range(E_local) if experts is None else experts):
         ge = int(local_expert_offset) + le

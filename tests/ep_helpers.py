@@ -1,0 +1,115 @@
+"""Expected results of the expert-parallel layer, built from the CPU oracle.
+
+The expert-parallel forward (15642_moe_b200/ep.py) returns, per token, the fp32 sum over owner
+ranks (ascending) of each owner's fp32 partial (the sum of its experts' weighted outputs in
+ascending expert order), rounded once to bf16. The layer oracle sums over all experts in
+ascending order and rounds once (reference/moe_ref.py:110-136 with every owned expert local);
+the two differ only in the association of the fp32 additions. Both are computed here from
+per-expert oracle outputs.
+"""
+from __future__ import annotations
+
+import numpy as np
+
+H = 7168
+
+
+def per_expert_outputs(pkg, oracle, cfg, experts) -> dict:
+    """fp32 [T, 7168] weighted output of each global expert in `experts` over all cfg.T tokens
+    (zero rows for tokens that did not pick it), each expert generated on its own."""
+    res = {}
+    for ge in sorted(set(int(g) for g in experts)):
+        inp = pkg.make_inputs(cfg.with_(E_local=1, local_expert_offset=ge), "cpu")
+        res[ge] = oracle.moe_forward(**oracle.to_numpy_inputs(inp), return_fp32=True)
+    return res
+
+
+def owned_picks(topk_row, world: int, e_rank: int) -> list[int]:
+    return sorted(int(g) for g in topk_row if 0 <= g < world * e_rank)
+
+
+def owner_partial(contrib: dict, topk_idx, t: int, d: int, world: int, e_rank: int):
+    """fp32 [7168] partial of owner d for token t (None if t picked none of d's experts)."""
+    picks = [g for g in owned_picks(topk_idx[t], world, e_rank) if g // e_rank == d]
+    if not picks:
+        return None
+    part = np.zeros(H, np.float32)
+    for g in picks:
+        part = part + contrib[g][t]
+    return part
+
+
+def ep_combine_bits(oracle, partials: list) -> np.ndarray:
+    """Final combine of one token: fp32 sum of the present owners' partials in ascending owner
+    order from +0, one bf16 rounding."""
+    acc = np.zeros(H, np.float32)
+    for p in partials:
+        if p is not None:
+            acc = acc + p
+    return oracle.f32_to_bf16_bits(acc)
+
+
+def ep_expected_bits(oracle, contrib: dict, topk_idx, tokens, world: int, e_rank: int) -> np.ndarray:
+    """bf16 bits [len(tokens), 7168] of the expert-parallel result."""
+    rows = [ep_combine_bits(oracle, [owner_partial(contrib, topk_idx, t, d, world, e_rank)
+                                     for d in range(world)]) for t in tokens]
+    return np.stack(rows) if rows else np.zeros((0, H), np.uint16)
+
+
+def layer_oracle_bits(oracle, contrib: dict, topk_idx, tokens, world: int, e_rank: int) -> np.ndarray:
+    """bf16 bits of the single-rounding layer oracle over all owned experts."""
+    out = np.zeros((len(tokens), H), np.float32)
+    for i, t in enumerate(tokens):
+        for g in owned_picks(topk_idx[t], world, e_rank):
+            out[i] = out[i] + contrib[g][t]
+    return oracle.f32_to_bf16_bits(out)
+
+
+def gloo_worker(rank: int, world: int, port: int, T_global: int, e_rank: int, seed: int) -> None:
+    """One gloo rank of the CPU emulation of the expert-parallel data flow: handle exchange,
+    token / expert partition, owner-side partials, exchange, source-side combine."""
+    import importlib
+    import os
+    import sys
+
+    import torch.distributed as dist
+
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+    pkg = importlib.import_module("15642_moe_b200")
+    ep = importlib.import_module("15642_moe_b200.ep")
+    from oracle import moe_oracle as oracle
+
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=world)
+    try:
+        blob = bytes([rank + 1]) * 64
+        handles = ep.exchange_handles(blob)
+        assert handles == [bytes([r + 1]) * 64 for r in range(world)], "handles out of rank order"
+
+        cfg = pkg.MoEConfig(T=T_global, E_local=1, seed=seed)
+        inp = pkg.make_inputs(cfg, "cpu")
+        idx, _ = oracle.route(inp["routing_logits"].numpy(), inp["routing_bias"].float().numpy(),
+                              cfg.routed_scaling_factor)
+        lo_e, hi_e = ep.expert_range(rank, e_rank)
+        mine = sorted({int(g) for g in idx.ravel() if lo_e <= g < hi_e})
+        assert all(ep.owner_of(g, world, e_rank) == rank for g in mine)
+        contrib = per_expert_outputs(pkg, oracle, cfg, mine)
+        # Owner side: one fp32 partial per (token, this owner), for every global token.
+        partials = {t: owner_partial(contrib, idx, t, rank, world, e_rank) for t in range(T_global)}
+        gathered = [None] * world
+        dist.all_gather_object(gathered, partials)
+        # Source side: combine the own tokens' partials in ascending owner order.
+        lo, hi = ep.token_range(T_global, world, rank)
+        out = [ep_combine_bits(oracle, [gathered[d][t] for d in range(world)]) for t in range(lo, hi)]
+        outs = [None] * world
+        dist.all_gather_object(outs, out)
+        if rank == 0:
+            got = np.stack([r for o in outs for r in o])
+            allx = sorted({int(g) for g in idx.ravel() if g < world * e_rank})
+            full = per_expert_outputs(pkg, oracle, cfg, allx)
+            tokens = list(range(T_global))
+            np.testing.assert_array_equal(got, ep_expected_bits(oracle, full, idx, tokens, world, e_rank))
+            ref = layer_oracle_bits(oracle, full, idx, tokens, world, e_rank)
+            r = oracle.check_tolerance(ref, got)
+            assert r["bad"] == 0, r
+    finally:
+        dist.destroy_process_group()
