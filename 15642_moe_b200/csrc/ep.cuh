@@ -186,7 +186,7 @@ __global__ void __launch_bounds__(32) ep_barrier_kernel(const __grid_constant__ 
   __syncwarp();
 }
 
-// Grid-stride over the received rows (one CTA of 448 threads x 16 columns per row): the fp32
+// Grid-stride over the received rows (one CTA of 448 threads per row): the fp32
 // sum of the row's local routes in ascending expert order from +0, stored into the source
 // rank's comb[rank][t].
 __global__ void __launch_bounds__(COMBINE_THREADS) ep_combine_send_kernel(const __grid_constant__ EpPeers peers, const __grid_constant__ EpLayout L,
@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(COMBINE_THREADS) ep_combine_send_kernel(const 
   const int* src_T = ep_at<int>(me, L.src_T);
   const int* tok_nr = ep_at<int>(me, L.tok_nr);
   const int* tok_route = ep_at<int>(me, L.tok_route);
-  const int c0 = threadIdx.x * 16;
+  const int tid = threadIdx.x;
   for (int i = blockIdx.x; i < L.r_cap; i += gridDim.x) {
     const int src = i / L.t_max, t = i - src * L.t_max;
     int tn = src_T[src];
@@ -211,19 +211,20 @@ __global__ void __launch_bounds__(COMBINE_THREADS) ep_combine_send_kernel(const 
     float acc[16];
 #pragma unroll
     for (int k = 0; k < 16; ++k) acc[k] = 0.0f;
-    add_routes(acc, partial, tok_route + static_cast<size_t>(i) * TOP_K, n, dense_base, L.e_rank, c0);
-    float* dst = ep_at<float>(peers.base[src], L.comb) + (static_cast<size_t>(rank) * L.t_max + t) * H + c0;
-    store_f32x16(dst, acc);
+    add_routes(acc, partial, tok_route + static_cast<size_t>(i) * TOP_K, n, dense_base, L.e_rank, tid);
+    float* dst = ep_at<float>(peers.base[src], L.comb) + (static_cast<size_t>(rank) * L.t_max + t) * H;
+    store_row_f32(dst, acc, tid);
   }
 }
 
-__device__ __forceinline__ void add_f32x16(float (&acc)[16], const float* p) {
-  const float4* q = reinterpret_cast<const float4*>(p);
-  float4 v[4];
+// Adds the fp32 row at `row` into acc (the combine kernels' column mapping).
+__device__ __forceinline__ void add_row_f32(float (&acc)[16], const float* row, int tid) {
+  const float4* q = reinterpret_cast<const float4*>(row) + tid;
+  float4 v[COMBINE_Q];
 #pragma unroll
-  for (int j = 0; j < 4; ++j) v[j] = __ldcs(q + j);
+  for (int j = 0; j < COMBINE_Q; ++j) v[j] = __ldcs(q + j * COMBINE_THREADS);
 #pragma unroll
-  for (int j = 0; j < 4; ++j) {
+  for (int j = 0; j < COMBINE_Q; ++j) {
     acc[4 * j + 0] = __fadd_rn(acc[4 * j + 0], v[j].x);
     acc[4 * j + 1] = __fadd_rn(acc[4 * j + 1], v[j].y);
     acc[4 * j + 2] = __fadd_rn(acc[4 * j + 2], v[j].z);
@@ -246,14 +247,14 @@ __global__ void __launch_bounds__(COMBINE_THREADS) ep_final_combine_kernel(const
     const int ge = topk_idx[static_cast<size_t>(t) * TOP_K + k];
     if (ge >= 0 && ge < owned) mask |= 1u << (ge / L.e_rank);
   }
-  const int c0 = threadIdx.x * 16;
+  const int tid = threadIdx.x;
   const float* comb = reinterpret_cast<const float*>(me + L.comb);
   float acc[16];
 #pragma unroll
   for (int k = 0; k < 16; ++k) acc[k] = 0.0f;
   for (int d = 0; d < L.world; ++d)
-    if (mask & (1u << d)) add_f32x16(acc, comb + (static_cast<size_t>(d) * L.t_max + t) * H + c0);
-  store_bf16x16(out + static_cast<size_t>(t) * H + c0, acc);
+    if (mask & (1u << d)) add_row_f32(acc, comb + (static_cast<size_t>(d) * L.t_max + t) * H, tid);
+  store_row_bf16(out + static_cast<size_t>(t) * H, acc, tid);
 }
 
 }  // namespace moe

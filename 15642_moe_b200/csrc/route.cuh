@@ -226,20 +226,25 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__
   }
 }
 
-constexpr int COMBINE_THREADS = H / 16;  // 448: each thread owns 16 consecutive columns
+constexpr int COMBINE_THREADS = H / 16;  // 448 threads x 16 columns per row
 
 __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&v);
 }
 
-// Adds a token's weighted expert outputs to acc[16] (columns c0..c0+15): `routes` holds n
-// entries (le << 16) | slot in ascending le, and route (le, slot) is row dense_base[le] + slot
-// of `partial` (dense_base written by the GEMM2 kernel, entry [E_local] = all routes). Each
-// entry is checked against the expert's row range before it addresses anything.
+// Row layout of the combine kernels: thread `tid` of a 448-thread CTA owns the four float4
+// column groups q = tid + 448 j (j = 0..3) of a 7168-wide row, i.e. columns 4q..4q+3; acc[4j + c]
+// is column 4q_j + c. A warp's access then covers 512 contiguous bytes per instruction.
+constexpr int COMBINE_Q = H / 4 / COMBINE_THREADS;  // 4 float4 groups per thread
+
+// Adds a token's weighted expert outputs to acc: `routes` holds n entries (le << 16) | slot in
+// ascending le, and route (le, slot) is row dense_base[le] + slot of `partial` (dense_base
+// written by the GEMM2 kernel, entry [E_local] = all routes). Each entry is checked against the
+// expert's row range before it addresses anything.
 __device__ __forceinline__ void add_routes(float (&acc)[16], const float* __restrict__ partial,
                                            const int* __restrict__ routes, int n,
-                                           const int* __restrict__ dense_base, int E_local, int c0) {
+                                           const int* __restrict__ dense_base, int E_local, int tid) {
 #pragma unroll
   for (int k = 0; k < TOP_K; ++k) {
     if (k < n) {
@@ -254,12 +259,12 @@ __device__ __forceinline__ void add_routes(float (&acc)[16], const float* __rest
         report_status(ST_BAD_INDEX);
         continue;
       }
-      const float4* src = reinterpret_cast<const float4*>(partial + static_cast<size_t>(row) * H + c0);
-      float4 p[4];
+      const float4* src = reinterpret_cast<const float4*>(partial + static_cast<size_t>(row) * H) + tid;
+      float4 p[COMBINE_Q];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) p[j] = __ldcs(src + j);
+      for (int j = 0; j < COMBINE_Q; ++j) p[j] = __ldcs(src + j * COMBINE_THREADS);
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
+      for (int j = 0; j < COMBINE_Q; ++j) {
         acc[4 * j + 0] = __fadd_rn(acc[4 * j + 0], p[j].x);
         acc[4 * j + 1] = __fadd_rn(acc[4 * j + 1], p[j].y);
         acc[4 * j + 2] = __fadd_rn(acc[4 * j + 2], p[j].z);
@@ -269,27 +274,20 @@ __device__ __forceinline__ void add_routes(float (&acc)[16], const float* __rest
   }
 }
 
-// Rounds acc[16] once to bf16 and stores the 32 bytes at dst.
-__device__ __forceinline__ void store_bf16x16(__nv_bfloat16* dst, const float (&acc)[16]) {
-  uint4 o0, o1;
-  o0.x = pack_bf16x2(acc[0], acc[1]);
-  o0.y = pack_bf16x2(acc[2], acc[3]);
-  o0.z = pack_bf16x2(acc[4], acc[5]);
-  o0.w = pack_bf16x2(acc[6], acc[7]);
-  o1.x = pack_bf16x2(acc[8], acc[9]);
-  o1.y = pack_bf16x2(acc[10], acc[11]);
-  o1.z = pack_bf16x2(acc[12], acc[13]);
-  o1.w = pack_bf16x2(acc[14], acc[15]);
-  uint4* d = reinterpret_cast<uint4*>(dst);
-  d[0] = o0;
-  d[1] = o1;
+// Rounds acc once to bf16 and stores it into the row at `row` (bf16 [7168]).
+__device__ __forceinline__ void store_row_bf16(__nv_bfloat16* row, const float (&acc)[16], int tid) {
+  uint2* d = reinterpret_cast<uint2*>(row) + tid;
+#pragma unroll
+  for (int j = 0; j < COMBINE_Q; ++j)
+    d[j * COMBINE_THREADS] = make_uint2(pack_bf16x2(acc[4 * j], acc[4 * j + 1]), pack_bf16x2(acc[4 * j + 2], acc[4 * j + 3]));
 }
 
-// Stores acc[16] unrounded (64 bytes at dst).
-__device__ __forceinline__ void store_f32x16(float* dst, const float (&acc)[16]) {
-  float4* d = reinterpret_cast<float4*>(dst);
+// Stores acc unrounded into the row at `row` (fp32 [7168]).
+__device__ __forceinline__ void store_row_f32(float* row, const float (&acc)[16], int tid) {
+  float4* d = reinterpret_cast<float4*>(row) + tid;
 #pragma unroll
-  for (int j = 0; j < 4; ++j) d[j] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
+  for (int j = 0; j < COMBINE_Q; ++j)
+    d[j * COMBINE_THREADS] = make_float4(acc[4 * j], acc[4 * j + 1], acc[4 * j + 2], acc[4 * j + 3]);
 }
 
 // One CTA per token: out[t] = sum over its local routes, ascending expert order, of the
@@ -303,15 +301,15 @@ __global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(const float* _
                                                                   int T, int E_local, OutT* __restrict__ out) {
   const int t = blockIdx.x;
   if (t >= T) return;
-  const int c0 = threadIdx.x * 16;
+  const int tid = threadIdx.x;
   float acc[16];
 #pragma unroll
   for (int i = 0; i < 16; ++i) acc[i] = 0.0f;
-  add_routes(acc, partial, token_route + static_cast<size_t>(t) * TOP_K, token_nr[t], dense_base, E_local, c0);
+  add_routes(acc, partial, token_route + static_cast<size_t>(t) * TOP_K, token_nr[t], dense_base, E_local, tid);
   if constexpr (sizeof(OutT) == 2)
-    store_bf16x16(out + static_cast<size_t>(t) * H + c0, acc);
+    store_row_bf16(out + static_cast<size_t>(t) * H, acc, tid);
   else
-    store_f32x16(out + static_cast<size_t>(t) * H + c0, acc);
+    store_row_f32(out + static_cast<size_t>(t) * H, acc, tid);
 }
 
 }  // namespace moe
