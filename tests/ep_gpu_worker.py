@@ -2,9 +2,10 @@
 torchrun, one process per GPU). Every case compares this rank's expert-parallel output with
 
   * the same layer computed on this GPU alone, slice by slice: for each owner d (ascending),
-    moe_forward_f32 over this rank's tokens with d's experts (local_expert_offset =
-    d * e_rank), summed in fp32 and rounded once - bit for bit (the expert-parallel result is
-    defined to be exactly that);
+    moe_forward_f32 over all ranks' tokens with d's experts (local_expert_offset =
+    d * e_rank), summed in fp32, rounded once, rows of this rank - bit for bit. Owner d's GEMMs
+    see exactly the routes that expert-parallel owner d receives, so both run the same tiles
+    and the same schedule;
   * for the small case, the single-rounding CPU layer oracle, within the reference tolerance.
 
 Prints EP_CASE_OK <name> per case; any mismatch raises (non-zero exit).
@@ -51,21 +52,24 @@ class Layer:
             del inp
         torch.cuda.synchronize()
 
-    def tokens(self, lo, hi):
+    def tokens(self, ranges):
+        """Rows of the global batch given as [(lo, hi), ...], concatenated in that order."""
         inp = self.inp
-        return dict(hidden=inp["hidden_states"][lo:hi].contiguous(),
-                    hs=inp["hidden_states_scale"][:, lo:hi].float().contiguous(),
-                    lg=inp["routing_logits"][lo:hi].float().contiguous(),
+        cat = lambda t, dim: torch.cat([t.narrow(dim, lo, hi - lo) for lo, hi in ranges], dim).contiguous()
+        return dict(hidden=cat(inp["hidden_states"], 0), hs=cat(inp["hidden_states_scale"], 1).float(),
+                    lg=cat(inp["routing_logits"], 0).float(),
                     b=inp["routing_bias"].float().reshape(-1).contiguous(),
                     rsf=float(inp["routed_scaling_factor"]))
 
-    def reference(self, tok):
+    def reference(self, tok, lo, hi):
+        """Rows [lo, hi) of the layer over all of `tok`'s tokens, slice by slice."""
         T = tok["hidden"].shape[0]
         acc = torch.zeros((T, 7168), dtype=torch.float32, device=tok["hidden"].device)
-        for s in self.slices:
-            acc += pkg.moe_forward(tok["hidden"], tok["hs"], s["w13p"], s["s13"], s["w2p"], s["s2"],
-                                   tok["lg"], tok["b"], tok["rsf"], s["offset"], fp32_out=True)
-        return acc.to(torch.bfloat16)
+        if T > 0:
+            for s in self.slices:
+                acc += pkg.moe_forward(tok["hidden"], tok["hs"], s["w13p"], s["s13"], s["w2p"], s["s2"],
+                                       tok["lg"], tok["b"], tok["rsf"], s["offset"], fp32_out=True)
+        return acc[lo:hi].to(torch.bfloat16)
 
     def ep_forward(self, ctx, tok, rank):
         s = self.slices[rank]
@@ -91,8 +95,8 @@ def case_layer(rank, world, device, T_global, e_rank, seed, skew=False, epochs=2
     cfg = base.with_(T=T_global, seed=seed)
     layer = Layer(cfg, world, e_rank, device)
     lo, hi = ep_mod.token_range(T_global, world, rank)
-    tok = layer.tokens(lo, hi)
-    ref = layer.reference(tok)
+    ref = layer.reference(layer.tokens([(0, T_global)]), lo, hi)
+    tok = layer.tokens([(lo, hi)])
     with ep_mod.ExpertParallel(t_rank_max=hi - lo, e_rank=e_rank, device=device) as ctx:
         for _ in range(epochs):               # repeated epochs reuse every buffer
             out = layer.ep_forward(ctx, tok, rank)
@@ -133,10 +137,11 @@ def case_ragged(rank, world, device):
     with ep_mod.ExpertParallel(t_rank_max=t_max, e_rank=e_rank, device=device) as ctx:
         for ep_i, counts in enumerate(plan):
             counts = [counts[r % len(counts)] for r in range(world)]
-            lo = rank * t_max
-            tok = layer.tokens(lo, lo + counts[rank])
+            ranges = [(r * t_max, r * t_max + counts[r]) for r in range(world)]
+            mine = sum(counts[:rank])
+            ref = layer.reference(layer.tokens(ranges), mine, mine + counts[rank])
+            tok = layer.tokens([ranges[rank]])
             out = layer.ep_forward(ctx, tok, rank)
-            ref = layer.reference(tok) if counts[rank] > 0 else out
             torch.cuda.synchronize()
             check_equal(f"ragged epoch {ep_i}", out, ref)
     check_status("ragged")
