@@ -55,6 +55,7 @@ CUDA_SIGNATURES = {
     "moe_ep_forward_profiled": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                         c_void_p, c_void_p, c_void_p, c_float, c_int, c_void_p,
                                         c_void_p, c_size_t, c_void_p, c_void_p]),
+    "moe_quantize_hidden": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
     "moe_synth_logits": (c_int, [c_void_p, c_uint64, c_int, c_int, c_void_p, c_void_p]),
     "moe_synth_bias": (c_int, [c_void_p, c_uint64, c_int, c_float, c_void_p, c_int, c_float,
                                c_void_p, c_void_p]),

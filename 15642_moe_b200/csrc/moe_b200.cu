@@ -19,6 +19,7 @@
 #include "gemm1.cuh"
 #include "gemm2.cuh"
 #include "pack.cuh"
+#include "quant.cuh"
 #include "synth.cuh"
 #include "moe_b200.h"
 
@@ -427,6 +428,21 @@ int moe_route(const float* logits, const float* bias, float routed_scaling_facto
       logits, bias, T, routed_scaling_factor, 0, 0, topk_idx, topk_w, nullptr, nullptr, nullptr,
       nullptr, nullptr);
   return cuda_check(cudaGetLastError(), "route_kernel launch");
+}
+
+int moe_quantize_hidden(const void* hidden_bf16, int T, void* out_e4m3, float* out_scale, void* stream) {
+  if (T < 0) return fail(MOE_ERR_INVALID, "moe_quantize_hidden: hidden must be [T, 7168]");
+  if (T == 0) return MOE_OK;
+  if (T > MAX_TOKENS) return fail(MOE_ERR_INVALID, "moe_quantize_hidden: T must be at most 65536");
+  if (!hidden_bf16 || !out_e4m3 || !out_scale) return fail(MOE_ERR_INVALID, "moe_quantize_hidden: null pointer argument");
+  if (!aligned16(hidden_bf16) || !aligned16(out_e4m3) || !aligned16(out_scale))
+    return fail(MOE_ERR_INVALID, "moe_quantize_hidden: every tensor must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  const size_t warps = static_cast<size_t>(T) * (HB / QB_PER_WARP);
+  quantize_hidden_kernel<<<grid_for(warps, 8, d->num_sms * 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
+      static_cast<const uint16_t*>(hidden_bf16), T, static_cast<uint8_t*>(out_e4m3), out_scale);
+  return cuda_check(cudaGetLastError(), "quantize_hidden launch");
 }
 
 int moe_synth_logits(const float* table, uint64_t seed, int T, int E, float* out, void* stream) {

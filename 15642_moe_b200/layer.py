@@ -135,6 +135,30 @@ def moe_forward(hidden, hidden_scale, W13_packed, W13_scale, W2_packed, W2_scale
     return out
 
 
+def quantize_hidden(hidden: torch.Tensor, out: torch.Tensor | None = None,
+                    scale: torch.Tensor | None = None):
+    """bf16 hidden [T, 7168] -> (e4m3 codes [T, 7168], fp32 scales [56, T]): per (token,
+    128-column block) scale = amax / 448, code = e4m3(x / scale) (the configurations'
+    quantisation), ready for moe_forward / run."""
+    _check(hidden.dim() == 2 and int(hidden.size(1)) == H, "hidden must be [T, 7168]")
+    _check(hidden.dtype == torch.bfloat16, "hidden must be bfloat16")
+    _check(hidden.is_contiguous(), "hidden must be contiguous")
+    _cuda(hidden, "hidden")
+    T, dev = int(hidden.size(0)), hidden.device
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=dev)
+    if scale is None:
+        scale = torch.empty((H_BLOCKS, T), dtype=torch.float32, device=dev)
+    _check(out.element_size() == 1 and tuple(out.shape) == (T, H) and out.is_contiguous(),
+           "out must be a contiguous FP8 [T, 7168] tensor")
+    _check(scale.dtype == torch.float32 and tuple(scale.shape) == (H_BLOCKS, T) and scale.is_contiguous(),
+           "scale must be a contiguous float32 [56, T] tensor")
+    with torch.cuda.device(dev):
+        _native.check(_native.cuda_lib().moe_quantize_hidden(hidden.data_ptr(), T, out.data_ptr(),
+                                                             scale.data_ptr(), _stream(dev)))
+    return out, scale
+
+
 def route(logits: torch.Tensor, bias: torch.Tensor, rsf: float):
     """(topk_idx int32 [T, 8], topk_w fp32 [T, 8]) from the device router."""
     _check(logits.dim() == 2 and logits.size(1) == E_GLOBAL and logits.dtype == torch.float32,

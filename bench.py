@@ -321,6 +321,18 @@ def bench_ours(args, rank, world, local_rank, dist):
     droof = roofline(dstages, kernel_work(drs, dcfg.T), peaks, load_traffic("decode_t64"))
     layer_bytes = drs["active"] * (W13_EXPERT_BYTES + W2_EXPERT_BYTES + W13_SCALE_BYTES + W2_SCALE_BYTES)
 
+    # FP8 activation quantiser (the step before the path), T = 16384: 352 MB moved per call,
+    # more than L2, so repeated calls stream from HBM.
+    TQ = 16384
+    xq = torch.randn((TQ, 7168), device=device).to(torch.bfloat16)
+    qo = torch.empty((TQ, 7168), dtype=torch.float8_e4m3fn, device=device)
+    qs = torch.empty((56, TQ), dtype=torch.float32, device=device)
+    for _ in range(3):
+        pkg.quantize_hidden(xq, qo, qs)
+    q_ms = time_steps(lambda: pkg.quantize_hidden(xq, qo, qs), 20) / 20
+    q_bytes = TQ * (7168 * 2 + 7168 + 56 * 4)
+    del xq, qo, qs
+
     e2e = e2e_run(pkg, inp, device, args.steps, args.warmup)
     if dist is not None:
         t = torch.tensor([e2e["ms_per_step"]], device=device)
@@ -358,6 +370,10 @@ def bench_ours(args, rank, world, local_rank, dist):
                        "weight_bytes": int(layer_bytes),
                        "hbm_frac_layer": round(layer_bytes / (dms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                        "roofline": droof, "stage_us": {k: round(v * 1e3, 2) for k, v in dstages.items()}},
+        "quantize": {"T": TQ, "us": round(q_ms * 1e3, 2), "bytes": q_bytes,
+                     "achieved_gbs": round(q_bytes / (q_ms * 1e-3) / 1e9, 1),
+                     "hbm_frac": round(q_bytes / (q_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                     "kernel": "quantize_hidden_kernel: bf16 [T,7168] -> e4m3 + [56,T] scales"},
         "e2e": {"value": round(cfg.T * world / (e2e["ms_per_step"] * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
                 "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],

@@ -141,6 +141,13 @@ int moe_route(const float* logits, const float* bias, float routed_scaling_facto
  * regions (15). For tests and tooling. */
 int moe_workspace_layout(int T, int E_local, size_t* offsets, int n);
 
+/* FP8 activation quantiser, the step before moe_forward: bf16 hidden [T, 7168] -> e4m3 codes
+ * [T, 7168] and block-major fp32 scales [56, T] (the layout reference/moe_ref.py:44-45 takes).
+ * Per (token, 128-column block): scale = amax / 448 (fp32 division; 1.0 for an all-zero block),
+ * code = e4m3(x / scale), round to nearest even, saturating to +-448. Inputs must be finite.
+ * No reference counterpart: the reference receives already-quantised activations. */
+int moe_quantize_hidden(const void* hidden_bf16, int T, void* out_e4m3, float* out_scale, void* stream);
+
 /* ---- Seeded synthetic inputs on the GPU (bit-identical to the CPU generator) ----
  * table: device fp32 [65537] inverse-normal-CDF table (see the Python package).
  * No reference counterpart: the reference draws inputs with torch (moe_layer.py:47-74). */

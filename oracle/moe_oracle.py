@@ -109,6 +109,34 @@ def route(logits: np.ndarray, bias: np.ndarray, rsf: float):
     return topk_idx, w
 
 
+# ---------------------------------------------------------------------------- quantiser
+def encode_e4m3(y: np.ndarray) -> np.ndarray:
+    """fp32 -> e4m3fn codes, round to nearest even, saturating to +-448 (NaN not produced)."""
+    y = np.asarray(y, np.float32)
+    pos = _e4m3_table()[:127].astype(np.float64)           # codes 0x00..0x7E, increasing
+    a = np.minimum(np.abs(y).astype(np.float64), 448.0)
+    i = np.clip(np.searchsorted(pos, a, side="right") - 1, 0, 126)
+    j = np.minimum(i + 1, 126)
+    lo, hi = pos[i], pos[j]
+    up = (a - lo > hi - a) | ((a - lo == hi - a) & (i % 2 == 1))
+    code = np.where(up & (j != i), j, i).astype(np.uint8)
+    return np.where(np.signbit(y), code | np.uint8(0x80), code).astype(np.uint8)
+
+
+def quantize_hidden(x: np.ndarray):
+    """bf16-valued fp32 [T, 7168] -> (e4m3 codes [T, 7168], fp32 scales [56, T]) with the
+    benchmark configurations' convention: per (token, 128-column block) scale = amax / 448
+    (1 for an all-zero block), code = e4m3(x / scale). Restates the quantisation the configs
+    apply to hidden states before reference/moe_ref.py:run (test infrastructure)."""
+    x = np.asarray(x, np.float32)
+    T = x.shape[0]
+    blk = x.reshape(T, H // BLOCK, BLOCK)
+    amax = np.abs(blk).max(axis=2)
+    scale = np.where(amax > 0, amax / np.float32(448.0), np.float32(1.0)).astype(np.float32)
+    codes = encode_e4m3(blk / scale[:, :, None])
+    return codes.reshape(T, H), np.ascontiguousarray(scale.T)
+
+
 # ---------------------------------------------------------------------------- expert compute
 def dequant_hidden(hidden_u8: np.ndarray, hidden_scale: np.ndarray) -> np.ndarray:
     """A = fp8(hidden) * scale[h/128, t] (moe_ref.py:59-67)."""
