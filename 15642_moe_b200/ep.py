@@ -9,11 +9,11 @@ synchronise through epoch flags in device memory. torch.distributed (NCCL or glo
 only at set-up, to all-gather the IPC handles, and for the host barriers around set-up and
 teardown.
 
-Per rank the result equals, bit for bit, the sum over owner ranks d in ascending order of
-``moe_forward(tokens, experts of d, local_expert_offset = d * e_rank)`` taken in fp32 and
-rounded once to bf16 (each owner's partial is itself rounded once to bf16, as moe_forward's
-output is). There is no counterpart in the reference, which runs one GPU with 32 local experts
-(kernels/moe.cu:744-900); each owner's share is exactly that computation.
+Per rank the result equals, bit for bit, the fp32 sum over owner ranks d in ascending order of
+``moe_forward(all tokens, experts of d, local_expert_offset = d * e_rank, fp32_out=True)``
+(the fp32 per-token sum before moe_forward's final rounding), restricted to the rank's tokens
+and rounded once to bf16. There is no counterpart in the reference, which runs one GPU with 32
+local experts (kernels/moe.cu:744-900); each owner's share is exactly that computation.
 """
 from __future__ import annotations
 
@@ -62,12 +62,27 @@ def exchange_handles(handle: bytes, group=None) -> list[bytes]:
     return [bytes(p.cpu().tolist()) for p in parts]
 
 
+def agree_shapes(t_rank_max: int, e_rank: int, group=None, device=None) -> list[tuple[int, int]]:
+    """(t_rank_max, e_rank) of every rank, in rank order (one all_gather)."""
+    import torch.distributed as dist
+    backend = dist.get_backend(group)
+    dev = (device if device is not None else torch.device("cuda", torch.cuda.current_device())) \
+        if backend == "nccl" else torch.device("cpu")
+    mine = torch.tensor([t_rank_max, e_rank], dtype=torch.int64, device=dev)
+    parts = [torch.empty_like(mine) for _ in range(dist.get_world_size(group))]
+    dist.all_gather(parts, mine, group=group)
+    return [(int(p[0]), int(p[1])) for p in parts]
+
+
 class ExpertParallel:
     """One rank's expert-parallel context (symmetric buffer, peer mappings, workspace).
 
-    ``t_rank_max``: most tokens any call on this rank passes; ``e_rank``: experts per rank
-    (default 256 // world). Without an initialised process group it runs as a single rank.
-    Use as a context manager or call ``close()`` on every rank.
+    ``t_rank_max``: most tokens any call on this rank passes (ranks may differ; every rank's
+    buffers are sized for the largest value over the group, since the layout of the peer
+    buffers must be identical); ``e_rank``: experts per rank (default 256 // world, the same on
+    every rank). Without an initialised process group it runs as a single rank. Collective:
+    every rank of the group constructs it; use as a context manager or call ``close()`` on
+    every rank.
     """
 
     def __init__(self, t_rank_max: int, e_rank: int | None = None, group=None,
@@ -79,18 +94,29 @@ class ExpertParallel:
         self.world = dist.get_world_size(group) if self.distributed else 1
         _check(1 <= self.world <= MAX_RANKS, "expert parallelism supports 1..8 ranks")
         self.e_rank = int(e_rank) if e_rank is not None else E_GLOBAL // self.world
-        self.t_rank_max = int(t_rank_max)
         self.device = torch.device("cuda", torch.cuda.current_device() if device is None else
                                    (device if isinstance(device, int) else device.index))
+        # All ranks agree on the buffer geometry before any of them allocates: the largest
+        # t_rank_max of the group, and one e_rank (every rank sees the same gathered values, so
+        # a mismatch raises on all of them and no rank is left waiting in a collective).
+        shapes = agree_shapes(int(t_rank_max), self.e_rank, group, self.device) if self.world > 1 \
+            else [(int(t_rank_max), self.e_rank)]
+        _check(len({e for _, e in shapes}) == 1, f"e_rank differs between ranks: {[e for _, e in shapes]}")
+        self.t_rank_max = max(1, max(t for t, _ in shapes))
         self.lib = _native.cuda_lib()
         self._ctx = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(_native.EP_HANDLE_BYTES)
         with torch.cuda.device(self.device):
-            _native.check(self.lib.moe_ep_create(self.rank, self.world, self.t_rank_max, self.e_rank,
-                                                 ctypes.byref(self._ctx), handle))
+            rc = self.lib.moe_ep_create(self.rank, self.world, self.t_rank_max, self.e_rank,
+                                        ctypes.byref(self._ctx), handle)
+            msg = self.lib.moe_last_error().decode(errors="replace") if rc else ""
+            # A failure on any rank fails every rank here, before anyone waits on a peer.
+            self._all_ok(rc == 0, f"moe_ep_create: {msg}")
             try:
                 handles = (exchange_handles(handle.raw, group) if self.world > 1 else [handle.raw])
-                _native.check(self.lib.moe_ep_connect(self._ctx, b"".join(handles)))
+                rc = self.lib.moe_ep_connect(self._ctx, b"".join(handles))
+                msg = self.lib.moe_last_error().decode(errors="replace") if rc else ""
+                self._all_ok(rc == 0, f"moe_ep_connect: {msg}")
             except BaseException:
                 self.lib.moe_ep_destroy(self._ctx)
                 self._ctx = None
@@ -99,6 +125,15 @@ class ExpertParallel:
             self.workspace = torch.empty((nbytes,), dtype=torch.uint8, device=self.device)
         if self.world > 1:
             dist.barrier(group)       # every rank mapped every buffer before any forward
+
+    def _all_ok(self, ok: bool, msg: str) -> None:
+        """Raise on every rank unless every rank reports ok (one all_gather)."""
+        flags = [ok]
+        if self.world > 1:
+            flags = [bool(t) for t, _ in agree_shapes(int(ok), self.e_rank, self.group, self.device)]
+        if not all(flags):
+            bad = [r for r, f in enumerate(flags) if not f]
+            raise _native.MoEError(msg if not ok else f"expert-parallel set-up failed on rank(s) {bad}")
 
     @property
     def expert_offset(self) -> int:

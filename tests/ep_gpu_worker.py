@@ -155,7 +155,7 @@ def main():
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
     device = torch.device("cuda", local)
-    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120), device_id=device)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=device)
     try:
         for name in args.cases.split(","):
             if name == "oracle":

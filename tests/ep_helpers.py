@@ -84,6 +84,8 @@ def gloo_worker(rank: int, world: int, port: int, T_global: int, e_rank: int, se
         blob = bytes([rank + 1]) * 64
         handles = ep.exchange_handles(blob)
         assert handles == [bytes([r + 1]) * 64 for r in range(world)], "handles out of rank order"
+        # Buffer geometry agreed across ranks: every rank sees every rank's (t_rank_max, e_rank).
+        assert ep.agree_shapes(rank + 3, e_rank) == [(r + 3, e_rank) for r in range(world)]
 
         cfg = pkg.MoEConfig(T=T_global, E_local=1, seed=seed)
         inp = pkg.make_inputs(cfg, "cpu")

@@ -105,7 +105,12 @@ def _run_worker(n, cases, timeout):
            os.path.join(HERE, "ep_gpu_worker.py"), "--cases", cases]
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     p = subprocess.run(["timeout", "-k", "30", str(timeout)] + cmd, capture_output=True, text=True, env=env)
-    tail = (p.stdout + p.stderr)[-4000:]
+    # The cases that passed, then the first traceback of any rank, then the launcher's tail.
+    lines = (p.stdout + p.stderr).splitlines()
+    ok = [ln for ln in lines if "EP_CASE_OK" in ln]
+    first = next((i for i, ln in enumerate(lines) if "Traceback" in ln), None)
+    tb = lines[first:first + 40] if first is not None else []
+    tail = "\n".join(ok + ["--- first traceback ---"] + tb + ["--- tail ---"]) + "\n" + (p.stdout + p.stderr)[-1500:]
     assert p.returncode == 0, tail
     for c in cases.split(","):
         for r in range(n):
