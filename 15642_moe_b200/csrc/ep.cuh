@@ -8,11 +8,13 @@
  * W buffers (its own plus the peers' through CUDA IPC) and passes their addresses as EpPeers.
  * A forward on rank r, epoch e (all ranks call it the same number of times):
  *
- *   route_kernel            top-8 of 256 for the own T_r tokens (topk only)
+ *   route_kernel            top-8 of 256 for the own T_r tokens; every pick of an owned
+ *                           expert claims a local slot (local atomics, as on one GPU)
+ *   ep_reserve_kernel       per owned expert with local picks: one system-scope atomic on
+ *                           the owner's count reserves a block of slots
  *   ep_dispatch_kernel      per token and owner rank d that it picked: its FP8 row and 56
- *                           scales -> d.recv[r * T_max + t]; per pick a slot of d's expert
- *                           list claimed with a system-scope atomic on d.counts, and the
- *                           (row, weight, slot) records that d's gather / GEMM2 / combine read
+ *                           scales -> d.recv[r * T_max + t]; per pick the (row, weight, slot)
+ *                           records that d's gather / GEMM2 / combine read
  *   ep_barrier_kernel       release flag d.arrive[r] = e on every d, acquire own arrive[*] >= e
  *   gather, GEMM1, GEMM2    unchanged single-GPU kernels over the received rows
  *                           (row index = src * T_max + t, W * T_max "tokens")
@@ -87,6 +89,11 @@ inline EpLayout make_ep_layout(int world, int t_max, int e_rank) {
   return L;
 }
 
+// moe_ep_forward's workspace: the single-GPU layout over W * t_max rows and E_rank experts (its
+// topk, token lists and per-expert slot lists, [owned, T] <= [E_rank, W * t_max], serve the
+// source side), then the source's local route counts and reserved slot bases, 256 ints each.
+constexpr size_t EP_WS_EXTRA = 2 * 1024;
+
 struct EpPeers {
   uint8_t* base[EP_MAX_RANKS];  // symmetric buffer of each rank, mapped into this process
 };
@@ -96,30 +103,60 @@ __host__ __device__ __forceinline__ T_* ep_at(uint8_t* base, size_t off) {
   return reinterpret_cast<T_*>(base + off);
 }
 
-// One warp per own token. Lanes 0-7 hold the token's picks; owner d = ge / E_rank (picks of
-// experts >= world * E_rank have no owner and are dropped, as moe_ref.py:115-116 drops
-// non-local experts).
+// One thread per owned global expert g with local routes: one system-scope atomic on the
+// owner's count reserves a block of local_counts[g] consecutive slots, base[g] = its first.
+// (One remote atomic per (source, expert) instead of one per route: a popular expert's count
+// would otherwise serialise hundreds of atomics arriving over NVLink.)
+__global__ void __launch_bounds__(256) ep_reserve_kernel(const __grid_constant__ EpPeers peers,
+                                                         const __grid_constant__ EpLayout L,
+                                                         const int* __restrict__ local_counts,
+                                                         int* __restrict__ base) {
+  const int owned = L.world * L.e_rank;
+  for (int g = threadIdx.x; g < owned; g += blockDim.x) {
+    const int c = local_counts[g];
+    if (c <= 0) continue;
+    const int d = g / L.e_rank, le = g - d * L.e_rank;
+    base[g] = atomicAdd_system(ep_at<int>(peers.base[d], L.counts) + le, c);
+  }
+}
+
+// One warp per own token. route_kernel (run over all owned experts) gave the token its local
+// picks in ascending global expert order, token_route[t * 8 + k] = (g << 16) | local slot, and
+// route_w[g * T + local slot] their weights; the owner of g is d = g / E_rank. Lane k < n
+// stores its pick into owner d's slot base[g] + local slot (row, weight, and the row's route
+// list entry at its position among the token's picks of d); then the row (read once into
+// registers) and its 56 scales are stored into every owner it picked.
 __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant__ EpPeers peers, const __grid_constant__ EpLayout L, int rank, int T,
                                                           const uint8_t* __restrict__ hidden,
                                                           const float* __restrict__ hidden_scale,
-                                                          const int* __restrict__ topk_idx,
-                                                          const float* __restrict__ topk_w) {
+                                                          const int* __restrict__ token_nr,
+                                                          const int* __restrict__ token_route,
+                                                          const float* __restrict__ route_w,
+                                                          const int* __restrict__ base) {
   if (blockIdx.x == 0 && threadIdx.x < L.world)
     ep_at<int>(peers.base[threadIdx.x], L.src_T)[rank] = T;
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
   const int owned = L.world * L.e_rank;
   for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < T; t += warps) {
-    const int ge = lane < TOP_K ? topk_idx[static_cast<size_t>(t) * TOP_K + lane] : -1;
-    const float w = lane < TOP_K ? topk_w[static_cast<size_t>(t) * TOP_K + lane] : 0.0f;
-    const int d = (ge >= 0 && ge < owned) ? ge / L.e_rank : -1;
+    const int n = min(max(token_nr[t], 0), TOP_K);
+    int g = -1, ls = 0;
+    if (lane < n) {
+      const unsigned packed = static_cast<unsigned>(token_route[static_cast<size_t>(t) * TOP_K + lane]);
+      g = static_cast<int>(packed >> 16);
+      ls = static_cast<int>(packed & 0xFFFFu);
+      if (g >= owned || ls >= T) {
+        report_status(ST_BAD_INDEX);
+        g = -1;
+      }
+    }
+    const int d = g >= 0 ? g / L.e_rank : -1;
     int pos = 0, nd = 0;
     unsigned mask = 0;
 #pragma unroll
     for (int j = 0; j < TOP_K; ++j) {
-      const int gj = __shfl_sync(0xffffffffu, ge, j);
       const int dj = __shfl_sync(0xffffffffu, d, j);
-      pos += (d >= 0 && dj == d && gj < ge) ? 1 : 0;
+      pos += (d >= 0 && j < lane && dj == d) ? 1 : 0;
       nd += (dj == lane) ? 1 : 0;
       mask |= dj >= 0 ? (1u << dj) : 0u;
     }
@@ -127,12 +164,12 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
     if (lane < L.world) ep_at<int>(peers.base[lane], L.tok_nr)[row] = nd;
     if (d >= 0) {
       uint8_t* pb = peers.base[d];
-      const int le = ge - d * L.e_rank;
-      const int slot = atomicAdd_system(ep_at<int>(pb, L.counts) + le, 1);
-      if (slot < L.r_cap) {
+      const int le = g - d * L.e_rank;
+      const int slot = base[g] + ls;
+      if (slot >= 0 && slot < L.r_cap) {
         const size_t i = static_cast<size_t>(le) * L.r_cap + slot;
         ep_at<int>(pb, L.route_token)[i] = row;
-        ep_at<float>(pb, L.route_w)[i] = w;
+        ep_at<float>(pb, L.route_w)[i] = route_w[static_cast<size_t>(g) * T + ls];
         ep_at<int>(pb, L.tok_route)[static_cast<size_t>(row) * TOP_K + pos] = (le << 16) | slot;
       } else {
         report_status(ST_BAD_INDEX);

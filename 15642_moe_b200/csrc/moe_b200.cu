@@ -298,8 +298,8 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
     if (!aligned16(q)) return fail(MOE_ERR_INVALID, "moe_ep_forward: every tensor must be 16-byte aligned");
   const EpLayout& L = c->L;
   const Workspace ws = make_workspace(L.r_cap, L.e_rank);
-  if (workspace_bytes < ws.total)
-    return fail(MOE_ERR_WORKSPACE, "workspace too small: need " + std::to_string(ws.total) + " bytes");
+  if (workspace_bytes < ws.total + EP_WS_EXTRA)
+    return fail(MOE_ERR_WORKSPACE, "workspace too small: need " + std::to_string(ws.total + EP_WS_EXTRA) + " bytes");
   int dev = -1;
   if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
   if (dev != c->device) return fail(MOE_ERR_INVALID, "moe_ep_forward: current device differs from the context's");
@@ -323,17 +323,28 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
                ws.tiles_max, L.e_rank, c_hi, c_lo, c_scale};
   Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, counts, L.r_cap,
                ws.tiles_max, L.e_rank, ep_at<float>(me, L.route_w), partial, dense_base};
+  // Source side: local slot claims over all owned experts (route_kernel with E_local = owned).
+  const int owned = L.world * L.e_rank;
+  int* local_counts = reinterpret_cast<int*>(W + ws.total);
+  int* reserve_base = reinterpret_cast<int*>(W + ws.total + EP_WS_EXTRA / 2);
+  int* token_nr = reinterpret_cast<int*>(W + ws.token_nr);
+  int* token_route = reinterpret_cast<int*>(W + ws.token_route);
+  int* route_token = reinterpret_cast<int*>(W + ws.route_token);
+  float* route_w = reinterpret_cast<float*>(W + ws.route_w);
   const unsigned epoch = ++c->epoch;
   auto mark = [&](int i) {
     if (events != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
   };
   mark(0);
+  if (int rc = cuda_check(cudaMemsetAsync(local_counts, 0, sizeof(int) * owned, st), "memset local counts")) return rc;
   if (T > 0)
-    route_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, routed_scaling_factor, 0, 0, topk_idx, topk_w,
-                                              nullptr, nullptr, nullptr, nullptr, nullptr);
+    route_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, routed_scaling_factor, 0, owned, topk_idx, topk_w,
+                                              local_counts, token_nr, token_route, route_token, route_w);
   mark(1);
+  ep_reserve_kernel<<<1, 256, 0, st>>>(c->peers, L, local_counts, reserve_base);
   ep_dispatch_kernel<<<grid_for(static_cast<size_t>(T), 8, d->num_sms * 8), 256, 0, st>>>(
-      c->peers, L, c->rank, T, static_cast<const uint8_t*>(hidden), hidden_scale, topk_idx, topk_w);
+      c->peers, L, c->rank, T, static_cast<const uint8_t*>(hidden), hidden_scale, token_nr, token_route, route_w,
+      reserve_base);
   mark(2);
   ep_barrier_kernel<<<1, 32, 0, st>>>(c->peers, L.arrive, c->rank, L.world, epoch);
   mark(3);
@@ -501,7 +512,7 @@ size_t moe_ep_symmetric_bytes(int world, int t_rank_max, int e_rank) {
 
 size_t moe_ep_workspace_bytes(int world, int t_rank_max, int e_rank) {
   if (ep_check_shape(world, t_rank_max, e_rank) != MOE_OK) return 0;
-  return make_workspace(world * t_rank_max, e_rank).total;
+  return make_workspace(world * t_rank_max, e_rank).total + EP_WS_EXTRA;
 }
 
 int moe_ep_create(int rank, int world, int t_rank_max, int e_rank, void** ctx, void* ipc_handle) {

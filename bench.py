@@ -482,6 +482,14 @@ def bench_ep(args, rank, world, local_rank, dist):
         work = kernel_work(rs, T_r)
         roof = roofline(stages, work, peaks, load_traffic("prefill_t4096") if rank == 0 else None)
 
+        # Every rank's load and stage times (the slowest rank sets the step).
+        names_all = list(stages)
+        mine_t = torch.tensor([rs["routes"], rs["active"]] + [stages[n] for n in names_all],
+                              dtype=torch.float64, device=device)
+        parts = [torch.empty_like(mine_t) for _ in range(world)]
+        dist.all_gather(parts, mine_t)
+        per_rank = [p.tolist() for p in parts]
+
         kw = {kk: v for kk, v in mine.items() if kk != "local_expert_offset"}
         e2e = e2e_run(pkg, kw, device, args.steps, args.warmup, call=ctx.run)
         t = torch.tensor([e2e["ms_per_step"]], device=device)
@@ -520,11 +528,15 @@ def bench_ep(args, rank, world, local_rank, dist):
         "layer_tokens_per_s": round(T_global * args.steps / (ms * 1e-3), 1),
         "roofline": roof,
         "stage_us_rank0": {kk: round(v * 1e3, 2) for kk, v in stages.items()},
+        "routes_per_rank": [int(p[0]) for p in per_rank],
+        "stage_us_slowest_rank": (lambda p: {"rank": per_rank.index(p), **{n: round(v * 1e3, 2) for n, v in
+                                                                             zip(names_all, p[2:])}})(
+            max(per_rank, key=lambda p: p[2 + names_all.index("gemm1_swiglu")] + p[2 + names_all.index("gemm2_weighted")])),
         "e2e": {"value": round(slices / (e2e["ms_per_step"] * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
                 "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
                 "ms_per_step": round(e2e["ms_per_step"], 4), "per": "rank 0 (max over ranks)"},
-        "gpu_launches": 9 * args.steps,
+        "gpu_launches": 10 * args.steps,
         "clocks": clocks,
         "device_status": status,
     }

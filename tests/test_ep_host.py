@@ -47,8 +47,9 @@ def test_capi_rejects_bad_ep_shapes(pkg):
     assert lib.moe_ep_workspace_bytes(2, 0, 128) == 0
     small = lib.moe_ep_symmetric_bytes(2, 16, 128)
     assert 0 < small < lib.moe_ep_symmetric_bytes(2, 4096, 128)
-    # The workspace is the single-GPU layout over world * t_rank_max received rows.
-    assert lib.moe_ep_workspace_bytes(8, 512, 32) == lib.moe_forward_workspace_bytes(4096, 32)
+    # The workspace is the single-GPU layout over world * t_rank_max received rows, plus the
+    # source side's local route counts and reserved slot bases (256 ints each).
+    assert lib.moe_ep_workspace_bytes(8, 512, 32) == lib.moe_forward_workspace_bytes(4096, 32) + 2048
     ctx = ctypes.c_void_p()
     handle = ctypes.create_string_buffer(64)
     assert lib.moe_ep_create(2, 2, 16, 128, ctypes.byref(ctx), handle) == 1
