@@ -26,9 +26,11 @@ __device__ __forceinline__ float sigmoid_rn(float x) {
   return __double2float_rn(d);
 }
 
-// Better-of for the top-k: larger value, ties to the lower index.
-__device__ __forceinline__ bool better(float v, int i, float ov, int oi) {
-  return ov > v || (ov == v && oi < i);
+// Order-preserving map of a float to an unsigned key (larger float -> larger key; +0 and -0
+// differ, which never matters here).
+__device__ __forceinline__ uint32_t order_key(float v) {
+  const uint32_t u = __float_as_uint(v);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
 // One warp per token; lane l owns experts 8l..8l+7, so a group of 32 experts is four lanes.
@@ -101,36 +103,39 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
   }
   const bool group_kept = rank < TOPK_GROUP;
 
-  // Top-8 of the biased scores inside the kept groups (moe_ref.py:99-101).
-  uint32_t taken = group_kept ? 0u : 0xFFu;
+  // Top-8 of the biased scores inside the kept groups (moe_ref.py:99-101). Each round is two
+  // hardware warp reductions: the largest order-preserving key, then the lowest expert index
+  // among the lanes holding it (ties to the lower index). Key 0 marks excluded or taken entries
+  // (below every real score's key; biased scores are never -0.0, so equal keys mean equal
+  // scores).
+  uint32_t key[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) key[i] = group_kept ? order_key(sb[i]) : 0u;
   int sel_idx[TOP_K];
   float sel_s[TOP_K];
 #pragma unroll
   for (int k = 0; k < TOP_K; ++k) {
-    float bv = -INFINITY, bs = 0.0f;
-    int bi = 0x7FFFFFFF;
+    uint32_t lk = 0;
+    int li = 0;
+    float ls = 0.0f;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      if (!((taken >> i) & 1u) && better(bv, bi, sb[i], lane * 8 + i)) {
-        bv = sb[i];
-        bi = lane * 8 + i;
-        bs = s[i];
+      if (key[i] > lk) {  // strict: the lower i keeps a tie
+        lk = key[i];
+        li = i;
+        ls = s[i];
       }
     }
+    const uint32_t mk = __reduce_max_sync(0xffffffffu, lk);
+    const uint32_t wi = __reduce_min_sync(0xffffffffu, lk == mk ? static_cast<uint32_t>(lane * 8 + li) : 0xFFFFFFFFu);
+    const float ws = __shfl_sync(0xffffffffu, ls, static_cast<int>(wi >> 3));
+    if (static_cast<int>(wi >> 3) == lane) {
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-      float ov = __shfl_xor_sync(0xffffffffu, bv, off);
-      int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-      float os = __shfl_xor_sync(0xffffffffu, bs, off);
-      if (better(bv, bi, ov, oi)) {
-        bv = ov;
-        bi = oi;
-        bs = os;
-      }
+      for (int i = 0; i < 8; ++i)
+        if (i == static_cast<int>(wi & 7u)) key[i] = 0u;
     }
-    if ((bi >> 3) == lane) taken |= 1u << (bi & 7);
-    sel_idx[k] = bi;
-    sel_s[k] = bs;
+    sel_idx[k] = static_cast<int>(wi);
+    sel_s[k] = ws;
   }
 
   // Weights: unbiased scores renormalised over the 8 picks, times the scaling factor
