@@ -217,17 +217,26 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__
       report_status(ST_BAD_INDEX);
       continue;
     }
+    // All 14 row loads and both scale loads are issued before any store (one round trip).
     const uint4* src = reinterpret_cast<const uint4*>(hidden + static_cast<size_t>(tok) * H);
     uint8_t* dst = a_tiled + static_cast<size_t>(tile) * HB * TILE_BYTES;
-#pragma unroll 2
-    for (int q = lane; q < H / 16; q += 32) {
-      const int kb = q >> 3, c = q & 7;
-      *reinterpret_cast<uint4*>(dst + static_cast<size_t>(kb) * TILE_BYTES + r * 128 +
-                                ((c ^ (r & 7)) << 4)) = __ldg(src + q);
+    uint4 v[H / 16 / 32];
+#pragma unroll
+    for (int i = 0; i < H / 16 / 32; ++i) v[i] = __ldg(src + lane + 32 * i);
+    float s0 = 0.0f, s1 = 0.0f;
+    if (lane < HB / 2) {
+      s0 = __ldg(hidden_scale + static_cast<size_t>(lane) * T + tok);
+      s1 = __ldg(hidden_scale + static_cast<size_t>(lane + HB / 2) * T + tok);
     }
-    for (int kb = lane; kb < HB; kb += 32)
-      a_scale[(static_cast<size_t>(tile) * HB + kb) * TILE_M + r] =
-          __ldg(hidden_scale + static_cast<size_t>(kb) * T + tok);
+#pragma unroll
+    for (int i = 0; i < H / 16 / 32; ++i) {
+      const int q = lane + 32 * i, kb = q >> 3, c = q & 7;
+      *reinterpret_cast<uint4*>(dst + static_cast<size_t>(kb) * TILE_BYTES + r * 128 + ((c ^ (r & 7)) << 4)) = v[i];
+    }
+    if (lane < HB / 2) {
+      a_scale[(static_cast<size_t>(tile) * HB + lane) * TILE_M + r] = s0;
+      a_scale[(static_cast<size_t>(tile) * HB + lane + HB / 2) * TILE_M + r] = s1;
+    }
   }
 }
 
