@@ -46,11 +46,13 @@ constexpr int EP_MAX_RANKS = 8;
 
 struct EpLayout {
   int world, t_max, e_rank, r_cap;  // r_cap = world * t_max received-row slots
-  size_t arrive, done, src_T, counts, recv_rows, recv_scale, route_token, route_w, tok_nr,
+  size_t epoch, arrive, done, src_T, counts, recv_rows, recv_scale, route_token, route_w, tok_nr,
       tok_route, comb, total;
 };
 
 // Byte offsets of the symmetric buffer (identical on every rank).
+//   epoch        u32                 this rank's forward count (read and advanced on the device,
+//                                    so a captured CUDA graph can be replayed)
 //   arrive/done  u32 [8]             epoch flags, index = signalling rank
 //   src_T        int [8]             tokens each source sent this epoch
 //   counts       int [E_rank]        routes per local expert (claimed by remote atomics)
@@ -74,6 +76,7 @@ inline EpLayout make_ep_layout(int world, int t_max, int e_rank) {
     off = ws_align(off + bytes);
     return o;
   };
+  L.epoch = take(sizeof(unsigned));
   L.arrive = take(sizeof(unsigned) * EP_MAX_RANKS);
   L.done = take(sizeof(unsigned) * EP_MAX_RANKS);
   L.src_T = take(sizeof(int) * EP_MAX_RANKS);
@@ -201,12 +204,21 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
   }
 }
 
-// One warp: lane d < world publishes `epoch` into rank d's flag slot [rank] (after a
-// system-scope fence, so every store this rank issued before this kernel is visible first),
-// then lane j < world waits, bounded, until this rank's flag [j] reaches `epoch`.
-__global__ void __launch_bounds__(32) ep_barrier_kernel(const __grid_constant__ EpPeers peers, size_t flag_off, int rank,
-                                                        int world, unsigned epoch) {
+// One warp: lane d < world publishes this forward's epoch into rank d's flag slot [rank] (after
+// a system-scope fence, so every store this rank issued before this kernel is visible first),
+// then lane j < world waits, bounded, until this rank's flag [j] reaches the epoch. The epoch
+// lives in this rank's buffer: the first barrier of a forward (`advance`) increments it, the
+// second reads it, so no host value is baked into the launches.
+__global__ void __launch_bounds__(32) ep_barrier_kernel(const __grid_constant__ EpPeers peers, size_t flag_off,
+                                                        size_t epoch_off, int rank, int world, int advance) {
   const int lane = threadIdx.x;
+  unsigned* ep = ep_at<unsigned>(peers.base[rank], epoch_off);
+  unsigned epoch = 0;
+  if (lane == 0) {
+    epoch = *ep + (advance ? 1u : 0u);
+    if (advance) *ep = epoch;
+  }
+  epoch = __shfl_sync(0xffffffffu, epoch, 0);
   if (lane < world) {
     __threadfence_system();
     st_release_sys(ep_at<unsigned>(peers.base[lane], flag_off) + rank, epoch);

@@ -269,7 +269,6 @@ struct EpCtx {
   EpPeers peers{};
   bool opened[EP_MAX_RANKS] = {};  // peers[d] came from cudaIpcOpenMemHandle
   bool connected = false;
-  unsigned epoch = 0;
 };
 
 int ep_check_shape(int world, int t_rank_max, int e_rank) {
@@ -331,7 +330,6 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
   int* token_route = reinterpret_cast<int*>(W + ws.token_route);
   int* route_token = reinterpret_cast<int*>(W + ws.route_token);
   float* route_w = reinterpret_cast<float*>(W + ws.route_w);
-  const unsigned epoch = ++c->epoch;
   auto mark = [&](int i) {
     if (events != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
   };
@@ -346,7 +344,7 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
       c->peers, L, c->rank, T, static_cast<const uint8_t*>(hidden), hidden_scale, token_nr, token_route, route_w,
       reserve_base);
   mark(2);
-  ep_barrier_kernel<<<1, 32, 0, st>>>(c->peers, L.arrive, c->rank, L.world, epoch);
+  ep_barrier_kernel<<<1, 32, 0, st>>>(c->peers, L.arrive, L.epoch, c->rank, L.world, 1);
   mark(3);
   const size_t route_max = static_cast<size_t>(L.r_cap) * (L.e_rank < TOP_K ? L.e_rank : TOP_K);
   gather_kernel<<<grid_for(route_max, 8, d->num_sms * 8), 256, 0, st>>>(
@@ -361,7 +359,7 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
       c->peers, L, c->rank, partial, dense_base);
   if (int rc = cuda_check(cudaMemsetAsync(counts, 0, sizeof(int) * L.e_rank, st), "memset counts")) return rc;
   mark(7);
-  ep_barrier_kernel<<<1, 32, 0, st>>>(c->peers, L.done, c->rank, L.world, epoch);
+  ep_barrier_kernel<<<1, 32, 0, st>>>(c->peers, L.done, L.epoch, c->rank, L.world, 0);
   mark(8);
   if (T > 0)
     ep_final_combine_kernel<<<T, COMBINE_THREADS, 0, st>>>(me, L, T, topk_idx, static_cast<__nv_bfloat16*>(out_bf16));

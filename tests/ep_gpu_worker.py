@@ -147,6 +147,44 @@ def case_ragged(rank, world, device):
     check_status("ragged")
 
 
+def case_graph(rank, world, device):
+    """Each rank captures its expert-parallel forward in a CUDA graph and replays it with new
+    tokens; every replay is a new epoch of the device-side barriers."""
+    e_rank, t_max = 32, 64
+    cfg = pkg.CONFIGS[3].with_(T=t_max * world, seed=11)
+    layer = Layer(cfg, world, e_rank, device)
+    s = layer.slices[rank]
+    lo = rank * t_max
+    tok = layer.tokens([(lo, lo + t_max)])
+    st = {k: tok[k].clone() for k in ("hidden", "hs", "lg")}
+    out = torch.empty((t_max, 7168), dtype=torch.bfloat16, device=device)
+    with ep_mod.ExpertParallel(t_rank_max=t_max, e_rank=e_rank, device=device) as ctx:
+        call = lambda: ctx.forward(st["hidden"], st["hs"], s["w13p"], s["s13"], s["w2p"], s["s2"], st["lg"],
+                                   tok["b"], tok["rsf"], out=out)
+        call()
+        torch.cuda.synchronize()
+        dist.barrier()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            call()
+        for seed in (12, 13, 14):
+            other = Layer.__new__(Layer)
+            other.inp = pkg.make_inputs(cfg.with_(seed=seed, E_local=1), device)
+            other.slices = layer.slices
+            new = other.tokens([(lo, lo + t_max)])
+            for k in ("hidden", "hs", "lg"):
+                st[k].copy_(new[k])
+            dist.barrier()
+            g.replay()
+            torch.cuda.synchronize()
+            everyone = other.tokens([(0, t_max * world)])
+            everyone["b"] = tok["b"]                    # the captured call keeps the first bias
+            ref = other.reference(everyone, lo, lo + t_max)
+            check_equal(f"graph replay seed {seed}", out, ref)
+        del g
+    check_status("graph")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--cases", default="oracle,ragged,weak,layer")
@@ -166,6 +204,8 @@ def main():
                 case_layer(rank, world, device, 4096, 32, seed=0)
             elif name == "layer":            # configuration 3: T = 8192, 256 / world experts each
                 case_layer(rank, world, device, 8192, 256 // world, seed=0)
+            elif name == "graph":
+                case_graph(rank, world, device)
             elif name == "skew":             # configuration 4's skewed routing, 256 / world each
                 case_layer(rank, world, device, 16384 if world == 8 else 4096, 256 // world, seed=0,
                            skew=True)

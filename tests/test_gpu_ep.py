@@ -119,9 +119,9 @@ def _run_worker(n, cases, timeout):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_two_ranks():
-    _run_worker(2, "oracle,ragged,weak,layer,skew", 900)
+    _run_worker(2, "oracle,ragged,weak,layer,skew,graph", 900)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 8, reason="needs 8 GPUs")
 def test_eight_ranks():
-    _run_worker(8, "oracle,ragged,weak,layer,skew", 1200)
+    _run_worker(8, "oracle,ragged,weak,layer,skew,graph", 1200)
