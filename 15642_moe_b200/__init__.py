@@ -9,19 +9,22 @@ Public surface (mirrors the reference's Python API):
   pack_w13 / pack_w2 / moe_forward  the extension functions of kernels/moe.cu:902-909
   route(logits, bias, rsf)       the device router alone (expert indices + weights)
   quantize_hidden(x_bf16)        FP8 activation quantiser (e4m3 codes + [56, T] block scales)
+  shared_expert_forward(...)     DeepSeek-V3 shared expert (all tokens, weight 1) on the same kernels
   make_inputs(cfg, device)       seeded synthetic inputs of the benchmark configurations
   ExpertParallel                 expert-parallel layer over the GPUs of one node (ep.py)
+  save_packed / load_packed      packed weights on disk (packed_io.py)
 """
 from .layer import (_cached_pack, _load_custom_ops, moe_forward, ops, pack_w13, pack_w2,
-                    quantize_hidden, route, run, run_custom, workspace_bytes)
+                    quantize_hidden, route, run, run_custom, shared_expert_forward, workspace_bytes)
 from .synth import CONFIGS, MoEConfig, make_inputs, quantile_table
 from ._native import MoEError, device_status, workspace_layout
 from .ep import ExpertParallel, expert_range, owner_of, token_range
+from .packed_io import load_packed, save_packed
 
 __all__ = [
     "run", "run_custom", "ops", "pack_w13", "pack_w2", "moe_forward", "route", "workspace_bytes",
-    "quantize_hidden",
+    "quantize_hidden", "shared_expert_forward",
     "make_inputs", "MoEConfig", "CONFIGS", "quantile_table", "MoEError", "device_status",
     "workspace_layout", "_cached_pack", "_load_custom_ops", "ExpertParallel", "expert_range",
-    "owner_of", "token_range",
+    "owner_of", "token_range", "save_packed", "load_packed",
 ]

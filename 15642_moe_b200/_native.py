@@ -35,6 +35,8 @@ CUDA_SIGNATURES = {
     "moe_forward_f32": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                 c_void_p, c_float, c_int, c_int, c_int, c_void_p, c_void_p, c_size_t,
                                 c_void_p]),
+    "moe_shared_expert_forward": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+                                          c_void_p, c_int, c_void_p, c_size_t, c_void_p]),
     "moe_forward_noalloc": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                                     c_void_p, c_void_p, c_float, c_int, c_int, c_int, c_void_p,
                                     c_void_p]),

@@ -191,13 +191,14 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
                  const float* w13_scale, const void* w2_packed, const float* w2_scale,
                  const float* logits, const float* bias, float routed_scaling_factor,
                  int local_expert_offset, int T, int E_local, void* out_bf16, void* workspace,
-                 size_t workspace_bytes, void* stream, void* const* events, bool out_f32 = false) {
+                 size_t workspace_bytes, void* stream, void* const* events, bool out_f32 = false,
+                 bool shared = false) {
   if (T < 0) return fail(MOE_ERR_INVALID, "hidden must be [T, 7168]");
   if (E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "W13_packed must be [E_local, ...] with 1 <= E_local <= 256");
   if (T == 0) return MOE_OK;
   if (T > MAX_TOKENS) return fail(MOE_ERR_INVALID, "moe_forward: T must be at most 65536");
-  if (!hidden || !hidden_scale || !w13_packed || !w13_scale || !w2_packed || !w2_scale || !logits ||
-      !bias || !out_bf16 || !workspace)
+  if (!hidden || !hidden_scale || !w13_packed || !w13_scale || !w2_packed || !w2_scale ||
+      (!shared && (!logits || !bias)) || !out_bf16 || !workspace)
     return fail(MOE_ERR_INVALID, "moe_forward: null pointer argument");
   const void* ptrs[] = {hidden, hidden_scale, w13_packed, w13_scale, w2_packed, w2_scale, logits, bias, out_bf16, workspace};
   for (const void* q : ptrs)
@@ -235,9 +236,13 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   };
   mark(0);
   if (int rc = cuda_check(cudaMemsetAsync(counts, 0, sizeof(int) * E_local, st), "memset counts")) return rc;
-  route_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, routed_scaling_factor, local_expert_offset,
-                                            E_local, topk_idx, topk_w, counts, token_nr, token_route,
-                                            route_token, route_w);
+  if (shared)
+    shared_route_kernel<<<grid_for(static_cast<size_t>(T), 256, d->num_sms * 4), 256, 0, st>>>(
+        T, counts, token_nr, token_route, route_token, route_w);
+  else
+    route_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, routed_scaling_factor, local_expert_offset,
+                                              E_local, topk_idx, topk_w, counts, token_nr, token_route,
+                                              route_token, route_w);
   mark(1);
   const size_t route_max = static_cast<size_t>(T) * (E_local < TOP_K ? E_local : TOP_K);
   gather_kernel<<<grid_for(route_max, 8, d->num_sms * 8), 256, 0, st>>>(
@@ -389,6 +394,13 @@ int moe_forward_f32(const void* hidden, const float* hidden_scale, const void* w
   return forward_impl(hidden, hidden_scale, w13_packed, w13_scale, w2_packed, w2_scale, logits, bias,
                       routed_scaling_factor, local_expert_offset, T, E_local, out_f32, workspace,
                       workspace_bytes, stream, nullptr, true);
+}
+
+int moe_shared_expert_forward(const void* hidden, const float* hidden_scale, const void* w13_packed,
+                              const float* w13_scale, const void* w2_packed, const float* w2_scale, int T,
+                              void* out, int out_fp32, void* workspace, size_t workspace_bytes, void* stream) {
+  return forward_impl(hidden, hidden_scale, w13_packed, w13_scale, w2_packed, w2_scale, nullptr, nullptr, 1.0f,
+                      0, T, 1, out, workspace, workspace_bytes, stream, nullptr, out_fp32 != 0, true);
 }
 
 int moe_forward_noalloc(const void* hidden, const float* hidden_scale, const void* w13_packed,

@@ -189,6 +189,22 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
   if (lane == 0 && token_nr != nullptr) token_nr[t] = nlocal;
 }
 
+// Routing of the shared expert: every token is slot t of the single local expert, weight 1.
+// Replaces route_kernel when the forward computes DeepSeek-V3's shared-expert branch.
+__global__ void __launch_bounds__(256) shared_route_kernel(int T, int* __restrict__ counts,
+                                                           int* __restrict__ token_nr,
+                                                           int* __restrict__ token_route,
+                                                           int* __restrict__ route_token,
+                                                           float* __restrict__ route_w) {
+  if (blockIdx.x == 0 && threadIdx.x == 0) counts[0] = T;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < T; t += gridDim.x * blockDim.x) {
+    token_nr[t] = 1;
+    token_route[static_cast<size_t>(t) * TOP_K] = t;  // (expert 0 << 16) | slot t
+    route_token[t] = t;
+    route_w[t] = 1.0f;
+  }
+}
+
 // One warp per local route (dense index d over all experts' slot lists): the route's tile row
 // is tile_off[e] * 128 + slot. Rows of a tile past its expert's last route are not written;
 // every row of the expert GEMMs is independent and those rows' results are never stored.

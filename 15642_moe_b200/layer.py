@@ -135,6 +135,48 @@ def moe_forward(hidden, hidden_scale, W13_packed, W13_scale, W2_packed, W2_scale
     return out
 
 
+def shared_expert_forward(hidden, hidden_scale, W13_packed, W13_scale, W2_packed, W2_scale,
+                          fp32_out: bool = False, out: torch.Tensor | None = None,
+                          workspace: torch.Tensor | None = None) -> torch.Tensor:
+    """DeepSeek-V3 shared expert: every token through one FP8 block-scaled expert (packed with
+    pack_w13 / pack_w2, E = 1) with weight 1. bf16 [T, 7168], or fp32 with ``fp32_out`` (add it
+    to ``moe_forward(..., fp32_out=True)`` and round once for the full layer output)."""
+    _check(hidden.dim() == 2 and int(hidden.size(1)) == H and hidden.element_size() == 1,
+           "hidden must be FP8 [T, 7168]")
+    T, dev = int(hidden.size(0)), hidden.device
+    _check(tuple(hidden_scale.shape) == (H_BLOCKS, T) and hidden_scale.dtype == torch.float32,
+           "hidden_scale must be float32 [56, T]")
+    _check(tuple(W13_packed.shape) == (1, *W13_PACKED_SHAPE) and W13_packed.dtype == torch.uint8,
+           "W13_packed must be [1, 16, 56, 256, 128] from pack_w13")
+    _check(tuple(W2_packed.shape) == (1, *W2_PACKED_SHAPE) and W2_packed.dtype == torch.uint8,
+           "W2_packed must be [1, 28, 16, 256, 128] from pack_w2")
+    _check(tuple(W13_scale.shape) == (1, G1_BLOCKS, H_BLOCKS) and W13_scale.dtype == torch.float32,
+           "W13_scale must be float32 [1, 32, 56]")
+    _check(tuple(W2_scale.shape) == (1, H_BLOCKS, I_BLOCKS) and W2_scale.dtype == torch.float32,
+           "W2_scale must be float32 [1, 56, 16]")
+    for t, n in ((hidden, "hidden"), (hidden_scale, "hidden_scale"), (W13_packed, "W13_packed"),
+                 (W13_scale, "W13_scale"), (W2_packed, "W2_packed"), (W2_scale, "W2_scale")):
+        _check(t.is_contiguous(), f"{n} must be contiguous")
+        _cuda(t, n)
+    lib = _native.cuda_lib()
+    out_dtype = torch.float32 if fp32_out else torch.bfloat16
+    if out is None:
+        out = torch.empty((T, H), dtype=out_dtype, device=dev)
+    _check(out.dtype == out_dtype and tuple(out.shape) == (T, H) and out.is_contiguous(), "bad out tensor")
+    nbytes = int(lib.moe_forward_workspace_bytes(T, 1)) if T > 0 else 0
+    if workspace is None:
+        workspace = torch.empty((max(nbytes, 1),), dtype=torch.uint8, device=dev)
+    _check(workspace.numel() >= nbytes, f"workspace must hold {nbytes} bytes")
+    if T == 0:
+        return out
+    with torch.cuda.device(dev):
+        _native.check(lib.moe_shared_expert_forward(
+            hidden.data_ptr(), hidden_scale.data_ptr(), W13_packed.data_ptr(), W13_scale.data_ptr(),
+            W2_packed.data_ptr(), W2_scale.data_ptr(), T, out.data_ptr(), 1 if fp32_out else 0,
+            workspace.data_ptr(), workspace.numel(), _stream(dev)))
+    return out
+
+
 def quantize_hidden(hidden: torch.Tensor, out: torch.Tensor | None = None,
                     scale: torch.Tensor | None = None):
     """bf16 hidden [T, 7168] -> (e4m3 codes [T, 7168], fp32 scales [56, T]): per (token,

@@ -118,6 +118,17 @@ int moe_forward_f32(const void* hidden, const float* hidden_scale, const void* w
                     int local_expert_offset, int T, int E_local, float* out_f32, void* workspace,
                     size_t workspace_bytes, void* stream);
 
+/* DeepSeek-V3's shared-expert branch over the same FP8 block-scaled format: one expert
+ * (w13_packed / w2_packed from moe_pack_w13 / moe_pack_w2 with E_local = 1, scales [1, 32, 56] /
+ * [1, 56, 16]) applied to every token with weight 1, i.e. moe_forward's expert computation
+ * (reference/moe_ref.py:126-134) with all tokens routed to it. out: bf16 [T, 7168], or fp32 when
+ * out_fp32 != 0 (to add to moe_forward_f32's routed output before one final rounding).
+ * Workspace: moe_forward_workspace_bytes(T, 1). No reference counterpart (the reference's layer
+ * has no shared expert). */
+int moe_shared_expert_forward(const void* hidden, const float* hidden_scale, const void* w13_packed,
+                              const float* w13_scale, const void* w2_packed, const float* w2_scale, int T,
+                              void* out, int out_fp32, void* workspace, size_t workspace_bytes, void* stream);
+
 /* moe_forward that also records events[0..5] (cudaEvent_t) on `stream`: before the first
  * launch and after each of its five kernels (route, gather, gemm1, gemm2, combine), for
  * per-kernel timing. No reference counterpart (instrumentation only). */

@@ -224,6 +224,20 @@ def moe_forward(routing_logits, routing_bias, hidden_states, hidden_states_scale
     return res
 
 
+def shared_expert_forward(hidden_states, hidden_states_scale, gemm1_weights, gemm1_weights_scale,
+                          gemm2_weights, gemm2_weights_scale, return_fp32=False):
+    """DeepSeek-V3 shared expert: the expert computation of moe_ref.py:126-134 applied to every
+    token with weight 1 (one expert, E = 1 arrays). Test infrastructure."""
+    A = dequant_hidden(hidden_states, hidden_states_scale)
+    W13 = dequant_block(gemm1_weights[0], gemm1_weights_scale[0])
+    W2 = dequant_block(gemm2_weights[0], gemm2_weights_scale[0])
+    G1 = A @ W13.T
+    X1, X2 = G1[:, :I], G1[:, I:]
+    C = ((X2 / (np.float32(1.0) + np.exp(-X2))) * X1).astype(np.float32)
+    O = (C @ W2.T).astype(np.float32)
+    return O if return_fp32 else f32_to_bf16_bits(O)
+
+
 def to_numpy_inputs(inputs: dict) -> dict:
     """Convert the torch keyword inputs of reference.run to the numpy form used here."""
     import torch
