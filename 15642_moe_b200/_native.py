@@ -47,7 +47,7 @@ CUDA_SIGNATURES = {
     "moe_workspace_layout": (c_int, [c_int, c_int, c_size_t_p, c_int]),
     "moe_ep_symmetric_bytes": (c_size_t, [c_int, c_int, c_int]),
     "moe_ep_workspace_bytes": (c_size_t, [c_int, c_int, c_int]),
-    "moe_ep_create": (c_int, [c_int, c_int, c_int, c_int, ctypes.POINTER(c_void_p), c_void_p]),
+    "moe_ep_create": (c_int, [c_int, c_int, c_int, c_int, c_void_p, ctypes.POINTER(c_void_p), c_void_p]),
     "moe_ep_connect": (c_int, [c_void_p, c_void_p]),
     "moe_ep_destroy": (c_int, [c_void_p]),
     "moe_ep_info": (c_int, [c_void_p, c_int_p]),

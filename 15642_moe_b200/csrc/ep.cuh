@@ -1,6 +1,7 @@
 /*
- * Expert-parallel (EP) MoE layer: W ranks (one GPU each, W <= 8), rank r owns the global
- * experts [r * E_rank, (r + 1) * E_rank) and holds its own T_r tokens. Token dispatch and the
+ * Expert-parallel (EP) MoE layer: W ranks (one GPU each, W <= 8); rank r owns E_rank global
+ * experts given by a placement table (by default [r * E_rank, (r + 1) * E_rank); any assignment
+ * of distinct experts, e.g. one balanced by expected load) and holds its own T_r tokens. Token dispatch and the
  * return of expert outputs are peer stores over NVLink issued by these kernels; the only
  * host-side collective is the one-time exchange of CUDA IPC handles.
  *
@@ -8,10 +9,10 @@
  * W buffers (its own plus the peers' through CUDA IPC) and passes their addresses as EpPeers.
  * A forward on rank r, epoch e (all ranks call it the same number of times):
  *
- *   route_kernel            top-8 of 256 for the own T_r tokens; every pick of an owned
- *                           expert claims a local slot (local atomics, as on one GPU)
- *   ep_reserve_kernel       per owned expert with local picks: one system-scope atomic on
- *                           the owner's count reserves a block of slots
+ *   route_kernel            top-8 of 256 for the own T_r tokens; every pick claims a local
+ *                           slot of its expert (local atomics, as on one GPU)
+ *   ep_reserve_kernel       per expert with local picks and an owner (placement table): one
+ *                           system-scope atomic on the owner's count reserves a block of slots
  *   ep_dispatch_kernel      per token and owner rank d that it picked: its FP8 row and 56
  *                           scales -> d.recv[r * T_max + t]; per pick the (row, weight, slot)
  *                           records that d's gather / GEMM2 / combine read
@@ -46,13 +47,15 @@ constexpr int EP_MAX_RANKS = 8;
 
 struct EpLayout {
   int world, t_max, e_rank, r_cap;  // r_cap = world * t_max received-row slots
-  size_t epoch, arrive, done, src_T, counts, recv_rows, recv_scale, route_token, route_w, tok_nr,
+  size_t epoch, place, arrive, done, src_T, counts, recv_rows, recv_scale, route_token, route_w, tok_nr,
       tok_route, comb, total;
 };
 
 // Byte offsets of the symmetric buffer (identical on every rank).
 //   epoch        u32                 this rank's forward count (read and advanced on the device,
 //                                    so a captured CUDA graph can be replayed)
+//   place        int [256]           expert placement: (owner rank << 16) | local index of each
+//                                    global expert, -1 without an owner (same on every rank)
 //   arrive/done  u32 [8]             epoch flags, index = signalling rank
 //   src_T        int [8]             tokens each source sent this epoch
 //   counts       int [E_rank]        routes per local expert (claimed by remote atomics)
@@ -77,6 +80,7 @@ inline EpLayout make_ep_layout(int world, int t_max, int e_rank) {
     return o;
   };
   L.epoch = take(sizeof(unsigned));
+  L.place = take(sizeof(int) * E_GLOBAL);
   L.arrive = take(sizeof(unsigned) * EP_MAX_RANKS);
   L.done = take(sizeof(unsigned) * EP_MAX_RANKS);
   L.src_T = take(sizeof(int) * EP_MAX_RANKS);
@@ -92,10 +96,31 @@ inline EpLayout make_ep_layout(int world, int t_max, int e_rank) {
   return L;
 }
 
-// moe_ep_forward's workspace: the single-GPU layout over W * t_max rows and E_rank experts (its
-// topk, token lists and per-expert slot lists, [owned, T] <= [E_rank, W * t_max], serve the
-// source side), then the source's local route counts and reserved slot bases, 256 ints each.
-constexpr size_t EP_WS_EXTRA = 2 * 1024;
+// moe_ep_forward's workspace: the single-GPU layout over W * t_max rows and E_rank experts (the
+// owner side), then the source side: its local route counts and reserved slot bases (256 ints
+// each), its tokens' route lists ([t_max] counts, [t_max, 8] entries) and its per-expert slot
+// lists over all 256 experts ([256, t_max] tokens and weights).
+struct EpSourceWs {
+  size_t local_counts, base, token_nr, token_route, route_token, route_w, total;
+};
+inline EpSourceWs make_ep_source_ws(size_t start, int t_max) {
+  EpSourceWs w{};
+  size_t off = start;
+  auto take = [&](size_t bytes) {
+    size_t o = off;
+    off = ws_align(off + bytes);
+    return o;
+  };
+  const size_t t = static_cast<size_t>(t_max);
+  w.local_counts = take(sizeof(int) * E_GLOBAL);
+  w.base = take(sizeof(int) * E_GLOBAL);
+  w.token_nr = take(sizeof(int) * t);
+  w.token_route = take(sizeof(int) * TOP_K * t);
+  w.route_token = take(sizeof(int) * E_GLOBAL * t);
+  w.route_w = take(sizeof(float) * E_GLOBAL * t);
+  w.total = off;
+  return w;
+}
 
 struct EpPeers {
   uint8_t* base[EP_MAX_RANKS];  // symmetric buffer of each rank, mapped into this process
@@ -106,26 +131,36 @@ __host__ __device__ __forceinline__ T_* ep_at(uint8_t* base, size_t off) {
   return reinterpret_cast<T_*>(base + off);
 }
 
-// One thread per owned global expert g with local routes: one system-scope atomic on the
+// Owner rank and local index of global expert g from the placement table, or d = -1.
+__device__ __forceinline__ void ep_owner(const int* place, const EpLayout& L, int g, int& d, int& le) {
+  const int v = (g >= 0 && g < E_GLOBAL) ? place[g] : -1;
+  d = v >> 16;
+  le = v & 0xFFFF;
+  if (v < 0 || d >= L.world || le >= L.e_rank) d = -1;
+}
+
+// One thread per global expert g with local routes and an owner: one system-scope atomic on the
 // owner's count reserves a block of local_counts[g] consecutive slots, base[g] = its first.
 // (One remote atomic per (source, expert) instead of one per route: a popular expert's count
 // would otherwise serialise hundreds of atomics arriving over NVLink.)
 __global__ void __launch_bounds__(256) ep_reserve_kernel(const __grid_constant__ EpPeers peers,
-                                                         const __grid_constant__ EpLayout L,
+                                                         const __grid_constant__ EpLayout L, int rank,
                                                          const int* __restrict__ local_counts,
                                                          int* __restrict__ base) {
-  const int owned = L.world * L.e_rank;
-  for (int g = threadIdx.x; g < owned; g += blockDim.x) {
+  const int* place = ep_at<int>(peers.base[rank], L.place);
+  for (int g = threadIdx.x; g < E_GLOBAL; g += blockDim.x) {
     const int c = local_counts[g];
-    if (c <= 0) continue;
-    const int d = g / L.e_rank, le = g - d * L.e_rank;
+    int d, le;
+    ep_owner(place, L, g, d, le);
+    if (c <= 0 || d < 0) continue;
     base[g] = atomicAdd_system(ep_at<int>(peers.base[d], L.counts) + le, c);
   }
 }
 
-// One warp per own token. route_kernel (run over all owned experts) gave the token its local
-// picks in ascending global expert order, token_route[t * 8 + k] = (g << 16) | local slot, and
-// route_w[g * T + local slot] their weights; the owner of g is d = g / E_rank. Lane k < n
+// One warp per own token. route_kernel (run over all 256 experts) gave the token its picks in
+// ascending global expert order, token_route[t * 8 + k] = (g << 16) | local slot, and
+// route_w[g * T + local slot] their weights; the owner of g comes from the placement table (picks
+// of experts without an owner are dropped, as moe_ref.py:115-116 drops non-local ones). Lane k < n
 // stores its pick into owner d's slot base[g] + local slot (row, weight, and the row's route
 // list entry at its position among the token's picks of d); then the row (read once into
 // registers) and its 56 scales are stored into every owner it picked.
@@ -140,7 +175,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
     ep_at<int>(peers.base[threadIdx.x], L.src_T)[rank] = T;
   const int lane = threadIdx.x & 31;
   const int warps = (gridDim.x * blockDim.x) >> 5;
-  const int owned = L.world * L.e_rank;
+  const int* place = ep_at<int>(peers.base[rank], L.place);
   for (int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < T; t += warps) {
     const int n = min(max(token_nr[t], 0), TOP_K);
     int g = -1, ls = 0;
@@ -148,12 +183,13 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
       const unsigned packed = static_cast<unsigned>(token_route[static_cast<size_t>(t) * TOP_K + lane]);
       g = static_cast<int>(packed >> 16);
       ls = static_cast<int>(packed & 0xFFFFu);
-      if (g >= owned || ls >= T) {
+      if (g >= E_GLOBAL || ls >= T) {
         report_status(ST_BAD_INDEX);
         g = -1;
       }
     }
-    const int d = g >= 0 ? g / L.e_rank : -1;
+    int d = -1, le = 0;
+    if (g >= 0) ep_owner(place, L, g, d, le);
     int pos = 0, nd = 0;
     unsigned mask = 0;
 #pragma unroll
@@ -167,7 +203,6 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
     if (lane < L.world) ep_at<int>(peers.base[lane], L.tok_nr)[row] = nd;
     if (d >= 0) {
       uint8_t* pb = peers.base[d];
-      const int le = g - d * L.e_rank;
       const int slot = base[g] + ls;
       if (slot >= 0 && slot < L.r_cap) {
         const size_t i = static_cast<size_t>(le) * L.r_cap + slot;
@@ -289,12 +324,13 @@ __global__ void __launch_bounds__(COMBINE_THREADS) ep_final_combine_kernel(const
                                                                            __nv_bfloat16* __restrict__ out) {
   const int t = blockIdx.x;
   if (t >= T) return;
-  const int owned = L.world * L.e_rank;
+  const int* place = reinterpret_cast<const int*>(me + L.place);
   unsigned mask = 0;
 #pragma unroll
   for (int k = 0; k < TOP_K; ++k) {
-    const int ge = topk_idx[static_cast<size_t>(t) * TOP_K + k];
-    if (ge >= 0 && ge < owned) mask |= 1u << (ge / L.e_rank);
+    int d, le;
+    ep_owner(place, L, topk_idx[static_cast<size_t>(t) * TOP_K + k], d, le);
+    if (d >= 0) mask |= 1u << d;
   }
   const int tid = threadIdx.x;
   const float* comb = reinterpret_cast<const float*>(me + L.comb);

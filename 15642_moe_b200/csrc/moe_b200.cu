@@ -302,8 +302,9 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
     if (!aligned16(q)) return fail(MOE_ERR_INVALID, "moe_ep_forward: every tensor must be 16-byte aligned");
   const EpLayout& L = c->L;
   const Workspace ws = make_workspace(L.r_cap, L.e_rank);
-  if (workspace_bytes < ws.total + EP_WS_EXTRA)
-    return fail(MOE_ERR_WORKSPACE, "workspace too small: need " + std::to_string(ws.total + EP_WS_EXTRA) + " bytes");
+  const EpSourceWs sw = make_ep_source_ws(ws.total, L.t_max);
+  if (workspace_bytes < sw.total)
+    return fail(MOE_ERR_WORKSPACE, "workspace too small: need " + std::to_string(sw.total) + " bytes");
   int dev = -1;
   if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
   if (dev != c->device) return fail(MOE_ERR_INVALID, "moe_ep_forward: current device differs from the context's");
@@ -327,24 +328,24 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
                ws.tiles_max, L.e_rank, c_hi, c_lo, c_scale};
   Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, counts, L.r_cap,
                ws.tiles_max, L.e_rank, ep_at<float>(me, L.route_w), partial, dense_base};
-  // Source side: local slot claims over all owned experts (route_kernel with E_local = owned).
-  const int owned = L.world * L.e_rank;
-  int* local_counts = reinterpret_cast<int*>(W + ws.total);
-  int* reserve_base = reinterpret_cast<int*>(W + ws.total + EP_WS_EXTRA / 2);
-  int* token_nr = reinterpret_cast<int*>(W + ws.token_nr);
-  int* token_route = reinterpret_cast<int*>(W + ws.token_route);
-  int* route_token = reinterpret_cast<int*>(W + ws.route_token);
-  float* route_w = reinterpret_cast<float*>(W + ws.route_w);
+  // Source side: local slot claims over all 256 experts (route_kernel with E_local = 256).
+  int* local_counts = reinterpret_cast<int*>(W + sw.local_counts);
+  int* reserve_base = reinterpret_cast<int*>(W + sw.base);
+  int* token_nr = reinterpret_cast<int*>(W + sw.token_nr);
+  int* token_route = reinterpret_cast<int*>(W + sw.token_route);
+  int* route_token = reinterpret_cast<int*>(W + sw.route_token);
+  float* route_w = reinterpret_cast<float*>(W + sw.route_w);
   auto mark = [&](int i) {
     if (events != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
   };
   mark(0);
-  if (int rc = cuda_check(cudaMemsetAsync(local_counts, 0, sizeof(int) * owned, st), "memset local counts")) return rc;
+  if (int rc = cuda_check(cudaMemsetAsync(local_counts, 0, sizeof(int) * E_GLOBAL, st), "memset local counts"))
+    return rc;
   if (T > 0)
-    route_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, routed_scaling_factor, 0, owned, topk_idx, topk_w,
+    route_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, routed_scaling_factor, 0, E_GLOBAL, topk_idx, topk_w,
                                               local_counts, token_nr, token_route, route_token, route_w);
   mark(1);
-  ep_reserve_kernel<<<1, 256, 0, st>>>(c->peers, L, local_counts, reserve_base);
+  ep_reserve_kernel<<<1, 256, 0, st>>>(c->peers, L, c->rank, local_counts, reserve_base);
   ep_dispatch_kernel<<<grid_for(static_cast<size_t>(T), 8, d->num_sms * 8), 256, 0, st>>>(
       c->peers, L, c->rank, T, static_cast<const uint8_t*>(hidden), hidden_scale, token_nr, token_route, route_w,
       reserve_base);
@@ -522,14 +523,24 @@ size_t moe_ep_symmetric_bytes(int world, int t_rank_max, int e_rank) {
 
 size_t moe_ep_workspace_bytes(int world, int t_rank_max, int e_rank) {
   if (ep_check_shape(world, t_rank_max, e_rank) != MOE_OK) return 0;
-  return make_workspace(world * t_rank_max, e_rank).total + EP_WS_EXTRA;
+  return make_ep_source_ws(make_workspace(world * t_rank_max, e_rank).total, t_rank_max).total;
 }
 
-int moe_ep_create(int rank, int world, int t_rank_max, int e_rank, void** ctx, void* ipc_handle) {
+int moe_ep_create(int rank, int world, int t_rank_max, int e_rank, const int* placement, void** ctx,
+                  void* ipc_handle) {
   if (ctx == nullptr || ipc_handle == nullptr) return fail(MOE_ERR_INVALID, "moe_ep_create: null pointer argument");
   *ctx = nullptr;
   if (int rc = ep_check_shape(world, t_rank_max, e_rank)) return rc;
   if (rank < 0 || rank >= world) return fail(MOE_ERR_INVALID, "moe_ep_create: rank must be in [0, world)");
+  // Placement table: global expert -> (owner << 16) | local index; -1 without an owner.
+  int place[E_GLOBAL];
+  for (int g = 0; g < E_GLOBAL; ++g) place[g] = -1;
+  for (int i = 0; i < world * e_rank; ++i) {
+    const int g = placement ? placement[i] : i;
+    if (g < 0 || g >= E_GLOBAL || place[g] != -1)
+      return fail(MOE_ERR_INVALID, "moe_ep_create: placement must list world * e_rank distinct experts in [0, 256)");
+    place[g] = ((i / e_rank) << 16) | (i % e_rank);
+  }
   static_assert(sizeof(cudaIpcMemHandle_t) == MOE_EP_HANDLE_BYTES, "IPC handle size");
   EpCtx* c = new EpCtx();
   c->rank = rank;
@@ -538,6 +549,9 @@ int moe_ep_create(int rank, int world, int t_rank_max, int e_rank, void** ctx, v
   int rc = cuda_check(cudaGetDevice(&c->device), "cudaGetDevice");
   if (!rc) rc = cuda_check(cudaMalloc(&c->local, c->L.total), "cudaMalloc(symmetric buffer)");
   if (!rc) rc = cuda_check(cudaMemset(c->local, 0, c->L.total), "cudaMemset(symmetric buffer)");
+  if (!rc)
+    rc = cuda_check(cudaMemcpy(c->local + c->L.place, place, sizeof(place), cudaMemcpyHostToDevice),
+                    "cudaMemcpy(placement)");
   cudaIpcMemHandle_t h{};
   if (!rc) rc = cuda_check(cudaIpcGetMemHandle(&h, c->local), "cudaIpcGetMemHandle");
   if (rc) {

@@ -1,7 +1,9 @@
 """Expert-parallel MoE layer over the GPUs of one node, one process per GPU.
 
-Rank r of a W-rank group owns the global experts [r * e_rank, (r + 1) * e_rank) (e_rank
-defaults to 256 / W, so W ranks hold the full 256-expert layer) and brings its own tokens.
+Rank r of a W-rank group owns e_rank global experts (e_rank defaults to 256 / W, so W ranks hold
+the full 256-expert layer): by default the contiguous range [r * e_rank, (r + 1) * e_rank), or
+the r-th list of an explicit placement (``balanced_placement`` spreads experts by expected load).
+Each rank brings its own tokens.
 ``ExpertParallel.forward`` returns, for those tokens, the layer output over every owned expert
 of every rank. The data path is the library's own kernels: token rows go to the owners and
 partial results come back as peer stores over NVLink (CUDA IPC mappings); the ranks
@@ -62,6 +64,23 @@ def exchange_handles(handle: bytes, group=None) -> list[bytes]:
     return [bytes(p.cpu().tolist()) for p in parts]
 
 
+def balanced_placement(loads, world: int, e_rank: int, experts=None) -> list[list[int]]:
+    """Assign `experts` (default 0 .. world * e_rank - 1) to `world` ranks, e_rank each, so the
+    ranks' summed expected loads (`loads[g]`, e.g. route counts of a calibration batch) are
+    close: largest load first, each to the least-loaded rank with room (ties to the lower rank).
+    Each rank's list is returned in ascending expert order."""
+    experts = list(range(world * e_rank)) if experts is None else [int(g) for g in experts]
+    _check(len(experts) == world * e_rank and len(set(experts)) == len(experts), "need world * e_rank distinct experts")
+    order = sorted(experts, key=lambda g: (-float(loads[g]), g))
+    bins = [[] for _ in range(world)]
+    total = [0.0] * world
+    for g in order:
+        d = min((r for r in range(world) if len(bins[r]) < e_rank), key=lambda r: (total[r], r))
+        bins[d].append(g)
+        total[d] += float(loads[g])
+    return [sorted(b) for b in bins]
+
+
 def agree_shapes(t_rank_max: int, e_rank: int, group=None, device=None) -> list[tuple[int, int]]:
     """(t_rank_max, e_rank) of every rank, in rank order (one all_gather)."""
     import torch.distributed as dist
@@ -86,7 +105,7 @@ class ExpertParallel:
     """
 
     def __init__(self, t_rank_max: int, e_rank: int | None = None, group=None,
-                 device: torch.device | int | None = None):
+                 device: torch.device | int | None = None, placement=None):
         import torch.distributed as dist
         self.group = group
         self.distributed = dist.is_available() and dist.is_initialized()
@@ -103,11 +122,22 @@ class ExpertParallel:
             else [(int(t_rank_max), self.e_rank)]
         _check(len({e for _, e in shapes}) == 1, f"e_rank differs between ranks: {[e for _, e in shapes]}")
         self.t_rank_max = max(1, max(t for t, _ in shapes))
+        if placement is None:
+            placement = [list(range(r * self.e_rank, (r + 1) * self.e_rank)) for r in range(self.world)]
+        _check(len(placement) == self.world and all(len(p) == self.e_rank for p in placement),
+               "placement must hold world lists of e_rank experts")
+        self.placement = [[int(g) for g in p] for p in placement]
+        flat = [g for p in self.placement for g in p]
+        if self.world > 1:       # every rank must use the same table
+            digest = int.from_bytes(__import__("hashlib").sha256(bytes(str(flat), "ascii")).digest()[:7], "little")
+            seen = agree_shapes(digest, self.e_rank, group, self.device)
+            _check(len({d for d, _ in seen}) == 1, "placement differs between ranks")
         self.lib = _native.cuda_lib()
         self._ctx = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(_native.EP_HANDLE_BYTES)
         with torch.cuda.device(self.device):
-            rc = self.lib.moe_ep_create(self.rank, self.world, self.t_rank_max, self.e_rank,
+            table = (ctypes.c_int * len(flat))(*flat)
+            rc = self.lib.moe_ep_create(self.rank, self.world, self.t_rank_max, self.e_rank, table,
                                         ctypes.byref(self._ctx), handle)
             msg = self.lib.moe_last_error().decode(errors="replace") if rc else ""
             # A failure on any rank fails every rank here, before anyone waits on a peer.
@@ -136,8 +166,9 @@ class ExpertParallel:
             raise _native.MoEError(msg if not ok else f"expert-parallel set-up failed on rank(s) {bad}")
 
     @property
-    def expert_offset(self) -> int:
-        return self.rank * self.e_rank
+    def experts(self) -> list[int]:
+        """Global experts of this rank, in the order of its weight arguments."""
+        return list(self.placement[self.rank])
 
     def forward(self, hidden, hidden_scale, W13_packed, W13_scale, W2_packed, W2_scale, logits, bias,
                 rsf: float, out: torch.Tensor | None = None, events=None) -> torch.Tensor:

@@ -153,3 +153,27 @@ def _make_gpu(cfg: MoEConfig, device: torch.device) -> dict:
                              w2.data_ptr(), s2.data_ptr(), st))
     return _kwargs(cfg, logits, bias, hidden.view(torch.float8_e4m3fn), hscale,
                    w13.view(torch.float8_e4m3fn), s13, w2.view(torch.float8_e4m3fn), s2)
+
+
+def make_weights(cfg: MoEConfig, experts, device: str | torch.device = "cuda") -> dict:
+    """W13 / W2 (e4m3) and their scales of the listed global experts, stacked in that order (for
+    a rank of an expert-parallel layer with an arbitrary placement); expert g is the same as in
+    any slice make_inputs generates."""
+    device = torch.device(device)
+    experts = [int(g) for g in experts]
+    E = len(experts)
+    lib = _native.cuda_lib()
+    with torch.cuda.device(device):
+        tab = _table_on(str(device))
+        st = torch.cuda.current_stream(device).cuda_stream
+        w13 = torch.empty((E, 2 * I_DIM, H), dtype=torch.uint8, device=device)
+        s13 = torch.empty((E, 2 * I_DIM // BLOCK, H // BLOCK), dtype=torch.float32, device=device)
+        w2 = torch.empty((E, H, I_DIM), dtype=torch.uint8, device=device)
+        s2 = torch.empty((E, H // BLOCK, I_DIM // BLOCK), dtype=torch.float32, device=device)
+        for i, g in enumerate(experts):
+            _native.check(lib.moe_synth_w13(tab.data_ptr(), cfg.seed, g, 1, cfg.weight_std, w13[i].data_ptr(),
+                                            s13[i].data_ptr(), st))
+            _native.check(lib.moe_synth_w2(tab.data_ptr(), cfg.seed, g, 1, cfg.weight_std, w2[i].data_ptr(),
+                                           s2[i].data_ptr(), st))
+    return dict(gemm1_weights=w13.view(torch.float8_e4m3fn), gemm1_weights_scale=s13,
+                gemm2_weights=w2.view(torch.float8_e4m3fn), gemm2_weights_scale=s2)

@@ -393,23 +393,20 @@ def bench_ours(args, rank, world, local_rank, dist):
     return line
 
 
-def ep_routing_stats(pkg, inp, rank: int, e_rank: int) -> dict:
-    """Routes and active experts that `rank` receives (picks of its experts over all tokens)."""
+def ep_routing_stats(pkg, inp, experts) -> dict:
+    """Routes and active experts a rank owning `experts` receives (their picks over all tokens)."""
     idx, _ = pkg.route(inp["routing_logits"], inp["routing_bias"], inp["routed_scaling_factor"])
-    idx = idx.cpu().numpy()
-    lo = rank * e_rank
-    local = (idx >= lo) & (idx < lo + e_rank)
-    counts = np.bincount((idx[local] - lo).ravel(), minlength=e_rank)
-    return dict(routes=int(local.sum()), active=int((counts > 0).sum()),
-                max_per_expert=int(counts.max()), tiles=int(((counts + 127) // 128).sum()))
+    per = np.bincount(idx.cpu().numpy().ravel(), minlength=256)[list(experts)]
+    return dict(routes=int(per.sum()), active=int((per > 0).sum()),
+                max_per_expert=int(per.max()), tiles=int(((per + 127) // 128).sum()))
 
 
 def bench_ep(args, rank, world, local_rank, dist):
     """Expert-parallel layer over `world` GPUs (weak scaling of configuration 2's per-GPU work).
 
-    Every rank owns 32 experts (rank r: experts 32r..32r+31, so N ranks hold 32N of the 256
-    and N = 8 is the full layer); the T = 4096 tokens of configuration 2 are split evenly over
-    the ranks. Each rank therefore streams the weights of 32 experts and receives, in
+    Every rank owns 32 experts (N ranks hold experts 0..32N-1 of the 256, spread by expected load
+    over the ranks; N = 8 is the full layer); the T = 4096 tokens of configuration 2 are split
+    evenly over the ranks. Each rank therefore streams the weights of 32 experts and receives, in
     expectation, the routes of 4096 token-slices, as the one GPU of configuration 2 does.
     `value` counts each token once per 32-expert slice it passes through (4096 * N per step),
     the unit configuration 2 is measured in at N = 1; `layer_tokens_per_s` is 4096 per step.
@@ -421,8 +418,15 @@ def bench_ep(args, rank, world, local_rank, dist):
     peaks = load_peaks()
     e_rank, T_global = 32, pkg.CONFIGS[2].T
     cfg = pkg.CONFIGS[2].with_(local_expert_offset=e_rank * rank)
-    inp = pkg.make_inputs(cfg, device)
-    rs = ep_routing_stats(pkg, inp, rank, e_rank)
+    inp = pkg.make_inputs(cfg.with_(E_local=1), device)
+    # Expert placement balanced by expected load: the route counts of a calibration batch (other
+    # tokens, seed 1, routed with this layer's bias) over the instantiated experts 0 .. 32N-1.
+    cal = pkg.make_inputs(cfg.with_(seed=1, E_local=1), device)["routing_logits"]
+    cidx, _ = pkg.route(cal, inp["routing_bias"], cfg.routed_scaling_factor)
+    loads = torch.bincount(cidx.flatten().long(), minlength=256).cpu().numpy()
+    placement = epm.balanced_placement(loads, world, e_rank, experts=range(e_rank * world))
+    inp.update(pkg.make_weights(cfg, placement[rank], device))
+    rs = ep_routing_stats(pkg, inp, placement[rank])
     lo, hi = epm.token_range(T_global, world, rank)
     mine = dict(inp)
     mine["hidden_states"] = inp["hidden_states"][lo:hi].contiguous()
@@ -434,7 +438,7 @@ def bench_ep(args, rank, world, local_rank, dist):
              s13=inp["gemm1_weights_scale"].float().contiguous(), s2=inp["gemm2_weights_scale"].float().contiguous(),
              lg=mine["routing_logits"].float().contiguous(), b=inp["routing_bias"].float().reshape(-1).contiguous())
     out = torch.empty((T_r, 7168), dtype=torch.bfloat16, device=device)
-    ctx = epm.ExpertParallel(t_rank_max=T_r, e_rank=e_rank, device=device)
+    ctx = epm.ExpertParallel(t_rank_max=T_r, e_rank=e_rank, device=device, placement=placement)
 
     def step(events=None):
         ctx.forward(k["hidden"], k["hs"], w13p, k["s13"], w2p, k["s2"], k["lg"], k["b"],
@@ -520,6 +524,8 @@ def bench_ep(args, rank, world, local_rank, dist):
                    "experts_per_rank": e_rank, "experts_instantiated": e_rank * world,
                    "experts_total": 256, "routed_scaling_factor": cfg.routed_scaling_factor,
                    "seed": cfg.seed, "parallelism": f"ep{world}: dispatch/combine as peer stores over NVLink",
+                   "placement": "experts 0..32N-1 balanced over the ranks by the route counts of a calibration "
+                                "batch (seed-1 tokens routed with this layer's bias)",
                    "token_count": "each token counted once per 32-expert slice it passes through "
                                   f"({T_global} x {world} per step); N=8 is the full 256-expert layer",
                    "routes_all_ranks": int(routes_all.item()), "routes_rank0": rs["routes"],

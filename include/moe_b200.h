@@ -174,9 +174,10 @@ int moe_synth_w2(const float* table, uint64_t seed, int e0, int E, float stddev,
 
 /* ---- Expert-parallel layer over W GPUs of one node (W <= 8), one process per GPU ----
  *
- * Rank r owns global experts [r * e_rank, (r + 1) * e_rank) (world * e_rank <= 256; picks of
- * experts beyond world * e_rank are dropped like non-local experts in reference/moe_ref.py:
- * 115-116) and holds its own tokens. moe_ep_forward returns, for the rank's own tokens, the
+ * Rank r owns e_rank global experts (world * e_rank <= 256): by default [r * e_rank,
+ * (r + 1) * e_rank), or any placement given at moe_ep_create (for example one balanced by
+ * expected load); picks of experts without an owner are dropped like non-local experts in
+ * reference/moe_ref.py:115-116. Each rank holds its own tokens. moe_ep_forward returns, for the rank's own tokens, the
  * layer output over all owned experts of all ranks: per owner rank the fp32 sum of its routes
  * in ascending expert order (moe_forward_f32's result for that rank's experts), then the fp32
  * sum of those partials in ascending rank order, rounded once to bf16. Token rows and fp32
@@ -202,8 +203,13 @@ size_t moe_ep_symmetric_bytes(int world, int t_rank_max, int e_rank);
 size_t moe_ep_workspace_bytes(int world, int t_rank_max, int e_rank);
 
 /* Creates rank `rank`'s context on the current device: allocates and zeroes the symmetric
- * buffer (synchronous) and writes its CUDA IPC handle (MOE_EP_HANDLE_BYTES) to ipc_handle. */
-int moe_ep_create(int rank, int world, int t_rank_max, int e_rank, void** ctx, void* ipc_handle);
+ * buffer (synchronous) and writes its CUDA IPC handle (MOE_EP_HANDLE_BYTES) to ipc_handle.
+ * placement: world * e_rank distinct global experts, rank-major (rank d owns
+ * placement[d * e_rank ...] in that local order, the order of its weight arguments), the same
+ * on every rank; NULL for the contiguous ranges [d * e_rank, (d + 1) * e_rank). Experts not
+ * listed have no owner and their picks are dropped. */
+int moe_ep_create(int rank, int world, int t_rank_max, int e_rank, const int* placement, void** ctx,
+                  void* ipc_handle);
 
 /* Maps the peers' buffers: handles = world * MOE_EP_HANDLE_BYTES, rank order. */
 int moe_ep_connect(void* ctx, const void* handles);

@@ -185,6 +185,43 @@ def case_graph(rank, world, device):
     check_status("graph")
 
 
+def case_placement(rank, world, device):
+    """Full layer with an interleaved placement (rank d owns the experts g with g % world == d).
+    Reference: each expert's fp32 contribution over all tokens (moe_forward_f32 with that expert
+    alone); owner d's partial is their sum in ascending expert order, the output the sum of the
+    partials in ascending owner order, rounded once."""
+    T_global, e_rank = 256, 256 // world
+    cfg = pkg.CONFIGS[3].with_(T=T_global, seed=21)
+    placement = [[g for g in range(256) if g % world == d] for d in range(world)]
+    inp = pkg.make_inputs(cfg.with_(E_local=1), device)
+    allt = dict(hidden=inp["hidden_states"], hs=inp["hidden_states_scale"].float().contiguous(),
+                lg=inp["routing_logits"].float().contiguous(), b=inp["routing_bias"].float().reshape(-1).contiguous(),
+                rsf=float(inp["routed_scaling_factor"]))
+    partial = []
+    for d in range(world):
+        acc = torch.zeros((T_global, 7168), dtype=torch.float32, device=device)
+        for g in placement[d]:
+            w = pkg.make_weights(cfg, [g], device)
+            acc += pkg.moe_forward(allt["hidden"], allt["hs"], pkg.pack_w13(w["gemm1_weights"]),
+                                   w["gemm1_weights_scale"], pkg.pack_w2(w["gemm2_weights"]),
+                                   w["gemm2_weights_scale"], allt["lg"], allt["b"], allt["rsf"], g, fp32_out=True)
+        partial.append(acc)
+    total = torch.zeros_like(partial[0])
+    for p_ in partial:
+        total += p_
+    lo, hi = ep_mod.token_range(T_global, world, rank)
+    ref = total[lo:hi].to(torch.bfloat16)
+    mine = pkg.make_weights(cfg, placement[rank], device)
+    with ep_mod.ExpertParallel(t_rank_max=hi - lo, e_rank=e_rank, device=device, placement=placement) as ctx:
+        out = ctx.forward(allt["hidden"][lo:hi].contiguous(), allt["hs"][:, lo:hi].contiguous(),
+                          pkg.pack_w13(mine["gemm1_weights"]), mine["gemm1_weights_scale"],
+                          pkg.pack_w2(mine["gemm2_weights"]), mine["gemm2_weights_scale"],
+                          allt["lg"][lo:hi].contiguous(), allt["b"], allt["rsf"])
+        torch.cuda.synchronize()
+    check_equal("interleaved placement", out, ref)
+    check_status("placement")
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--cases", default="oracle,ragged,weak,layer")
@@ -204,6 +241,8 @@ def main():
                 case_layer(rank, world, device, 4096, 32, seed=0)
             elif name == "layer":            # configuration 3: T = 8192, 256 / world experts each
                 case_layer(rank, world, device, 8192, 256 // world, seed=0)
+            elif name == "placement":
+                case_placement(rank, world, device)
             elif name == "graph":
                 case_graph(rank, world, device)
             elif name == "skew":             # configuration 4's skewed routing, 256 / world each

@@ -82,6 +82,25 @@ def test_single_rank_varying_T(pkg):
     assert pkg.device_status(reset=True) == 0
 
 
+def test_single_rank_permuted_placement(pkg):
+    """Experts held in reversed local order: the owner still sums a token's routes in ascending
+    global expert order, so the result equals moe_forward bit for bit."""
+    cfg = pkg.CONFIGS[1].with_(T=96, seed=12)
+    inp = pkg.make_inputs(cfg, "cuda")
+    k = _args(pkg, inp)
+    ref = _single(pkg, k)
+    order = list(range(31, -1, -1))
+    w = pkg.make_weights(cfg, order, "cuda")
+    kp = dict(k, w13p=pkg.pack_w13(w["gemm1_weights"]), s13=w["gemm1_weights_scale"],
+              w2p=pkg.pack_w2(w["gemm2_weights"]), s2=w["gemm2_weights_scale"])
+    with pkg.ExpertParallel(t_rank_max=96, e_rank=32, placement=[order]) as ctx:
+        assert ctx.experts == order
+        out = _ep(ctx, kp)
+        torch.cuda.synchronize()
+    np.testing.assert_array_equal(out_bits(out), out_bits(ref))
+    assert pkg.device_status(reset=True) == 0
+
+
 def test_run_surface(pkg):
     """ExpertParallel.run takes reference.run's keywords for the rank's tokens and experts."""
     cfg = pkg.CONFIGS[1].with_(T=32, seed=4)
@@ -119,9 +138,9 @@ def _run_worker(n, cases, timeout):
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
 def test_two_ranks():
-    _run_worker(2, "oracle,ragged,weak,layer,skew,graph", 900)
+    _run_worker(2, "oracle,ragged,weak,layer,skew,graph,placement", 900)
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 8, reason="needs 8 GPUs")
 def test_eight_ranks():
-    _run_worker(8, "oracle,ragged,weak,layer,skew,graph", 1200)
+    _run_worker(8, "oracle,ragged,weak,layer,skew,graph,placement", 1200)
