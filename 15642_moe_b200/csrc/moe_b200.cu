@@ -346,7 +346,9 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
                                               local_counts, token_nr, token_route, route_token, route_w);
   mark(1);
   ep_reserve_kernel<<<1, 256, 0, st>>>(c->peers, L, c->rank, local_counts, reserve_base);
-  ep_dispatch_kernel<<<grid_for(static_cast<size_t>(T), 8, d->num_sms * 8), 256, 0, st>>>(
+  // Two warps (tokens) per block, so small per-rank batches still spread their peer stores
+  // over every SM.
+  ep_dispatch_kernel<<<grid_for(static_cast<size_t>(T), 2, d->num_sms * 32), 64, 0, st>>>(
       c->peers, L, c->rank, T, static_cast<const uint8_t*>(hidden), hidden_scale, token_nr, token_route, route_w,
       reserve_base);
   mark(2);
