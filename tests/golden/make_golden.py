@@ -1,7 +1,7 @@
 """Generate the golden fixtures of tests/golden/ by running the REAL reference oracle.
 
 Run in the build container (where the reference checkout is mounted), from the repo root:
-    python tests/golden/make_golden.py [--reference PATH]
+    python tests/golden/make_golden.py --reference PATH_OF_THE_REFERENCE_CHECKOUT
 Nothing at test or benchmark time runs this script or reads the reference.
 
 For each case the inputs come from the package's seeded CPU generator (bit-identical to the
@@ -80,7 +80,7 @@ def run_reference(reference, inputs: dict, routing_only: bool):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--reference", default="/root/reference")
+    ap.add_argument("--reference", required=True, help="root of the reference checkout (contains reference/)")
     ap.add_argument("--only", default=None)
     args = ap.parse_args()
     sys.path.insert(0, args.reference)
