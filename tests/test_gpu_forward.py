@@ -79,6 +79,31 @@ def test_forward_t0(pkg):
     assert out.shape == (0, 7168)
 
 
+def test_max_tokens_rows_are_independent(pkg):
+    """At the largest T the API takes (65536), every token's output equals the output of a small
+    forward over just that token's row: routing and every GEMM row are per token, so the batch
+    around a token (tile membership, slot order, how many tiles each expert has) changes nothing.
+    Checked bit for bit on the first and last 300 tokens; one more token is refused."""
+    cfg = pkg.CONFIGS[2].with_(T=65536, seed=13)
+    inp = pkg.make_inputs(cfg, "cuda")
+    big = pkg.run(**inp)
+    torch.cuda.synchronize()
+    assert pkg.device_status(reset=True) == 0
+    for lo, hi in ((0, 300), (65536 - 300, 65536)):
+        part = dict(inp, hidden_states=inp["hidden_states"][lo:hi].contiguous(),
+                    hidden_states_scale=inp["hidden_states_scale"][:, lo:hi].contiguous(),
+                    routing_logits=inp["routing_logits"][lo:hi].contiguous())
+        small = pkg.run(**part)
+        np.testing.assert_array_equal(out_bits(big[lo:hi]), out_bits(small))
+    del big
+    x = torch.empty((65537, 7168), dtype=torch.uint8, device="cuda").view(torch.float8_e4m3fn)
+    with pytest.raises(RuntimeError, match="65536"):
+        pkg.moe_forward(x, torch.ones((56, 65537), device="cuda"), pkg.pack_w13(inp["gemm1_weights"][:1]),
+                        inp["gemm1_weights_scale"][:1].float().contiguous(), pkg.pack_w2(inp["gemm2_weights"][:1]),
+                        inp["gemm2_weights_scale"][:1].float().contiguous(), torch.zeros((65537, 256), device="cuda"),
+                        torch.zeros(256, device="cuda"), 2.5, 0)
+
+
 def test_stages(pkg, oracle):
     """Intermediate buffers of one run against numpy restatements."""
     cfg = pkg.MoEConfig(T=96, seed=6)
