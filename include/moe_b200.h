@@ -223,7 +223,8 @@ int moe_ep_info(void* ctx, int* out4);
 
 /* One expert-parallel layer forward for this rank's T <= t_rank_max tokens:
  *   hidden e4m3 [T, 7168], hidden_scale fp32 [56, T], logits fp32 [T, 256], bias fp32 [256],
- *   w13_packed / w2_packed: this rank's e_rank experts (moe_pack_w13 / moe_pack_w2),
+ *   w13_packed / w2_packed: this rank's e_rank experts in placement order (moe_pack_w13 /
+ *                 moe_pack_w2),
  *   w13_scale fp32 [e_rank, 32, 56], w2_scale fp32 [e_rank, 56, 16],
  *   out_bf16 bf16 [T, 7168]; workspace of moe_ep_workspace_bytes(world, t_rank_max, e_rank).
  * Asynchronous on `stream`; the call itself never waits for other ranks. No per-call host state:

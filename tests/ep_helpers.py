@@ -24,13 +24,22 @@ def per_expert_outputs(pkg, oracle, cfg, experts) -> dict:
     return res
 
 
-def owned_picks(topk_row, world: int, e_rank: int) -> list[int]:
-    return sorted(int(g) for g in topk_row if 0 <= g < world * e_rank)
+def owner_map(world: int, e_rank: int, placement=None) -> dict:
+    """Global expert -> owner rank (contiguous ranges unless a placement is given)."""
+    if placement is None:
+        placement = [range(d * e_rank, (d + 1) * e_rank) for d in range(world)]
+    return {int(g): d for d, experts in enumerate(placement) for g in experts}
 
 
-def owner_partial(contrib: dict, topk_idx, t: int, d: int, world: int, e_rank: int):
+def owned_picks(topk_row, world: int, e_rank: int, placement=None) -> list[int]:
+    own = owner_map(world, e_rank, placement)
+    return sorted(int(g) for g in topk_row if int(g) in own)
+
+
+def owner_partial(contrib: dict, topk_idx, t: int, d: int, world: int, e_rank: int, placement=None):
     """fp32 [7168] partial of owner d for token t (None if t picked none of d's experts)."""
-    picks = [g for g in owned_picks(topk_idx[t], world, e_rank) if g // e_rank == d]
+    own = owner_map(world, e_rank, placement)
+    picks = [g for g in owned_picks(topk_idx[t], world, e_rank, placement) if own[g] == d]
     if not picks:
         return None
     part = np.zeros(H, np.float32)
@@ -49,25 +58,29 @@ def ep_combine_bits(oracle, partials: list) -> np.ndarray:
     return oracle.f32_to_bf16_bits(acc)
 
 
-def ep_expected_bits(oracle, contrib: dict, topk_idx, tokens, world: int, e_rank: int) -> np.ndarray:
+def ep_expected_bits(oracle, contrib: dict, topk_idx, tokens, world: int, e_rank: int,
+                     placement=None) -> np.ndarray:
     """bf16 bits [len(tokens), 7168] of the expert-parallel result."""
-    rows = [ep_combine_bits(oracle, [owner_partial(contrib, topk_idx, t, d, world, e_rank)
+    rows = [ep_combine_bits(oracle, [owner_partial(contrib, topk_idx, t, d, world, e_rank, placement)
                                      for d in range(world)]) for t in tokens]
     return np.stack(rows) if rows else np.zeros((0, H), np.uint16)
 
 
-def layer_oracle_bits(oracle, contrib: dict, topk_idx, tokens, world: int, e_rank: int) -> np.ndarray:
+def layer_oracle_bits(oracle, contrib: dict, topk_idx, tokens, world: int, e_rank: int,
+                      placement=None) -> np.ndarray:
     """bf16 bits of the single-rounding layer oracle over all owned experts."""
     out = np.zeros((len(tokens), H), np.float32)
     for i, t in enumerate(tokens):
-        for g in owned_picks(topk_idx[t], world, e_rank):
+        for g in owned_picks(topk_idx[t], world, e_rank, placement):
             out[i] = out[i] + contrib[g][t]
     return oracle.f32_to_bf16_bits(out)
 
 
-def gloo_worker(rank: int, world: int, port: int, T_global: int, e_rank: int, seed: int) -> None:
+def gloo_worker(rank: int, world: int, port: int, T_global: int, e_rank: int, seed: int,
+                interleaved: bool = False) -> None:
     """One gloo rank of the CPU emulation of the expert-parallel data flow: handle exchange,
-    token / expert partition, owner-side partials, exchange, source-side combine."""
+    token / expert partition (contiguous expert ranges, or rank d owning the experts g with
+    g mod world == d), owner-side partials, exchange, source-side combine."""
     import importlib
     import os
     import sys
@@ -91,12 +104,16 @@ def gloo_worker(rank: int, world: int, port: int, T_global: int, e_rank: int, se
         inp = pkg.make_inputs(cfg, "cpu")
         idx, _ = oracle.route(inp["routing_logits"].numpy(), inp["routing_bias"].float().numpy(),
                               cfg.routed_scaling_factor)
-        lo_e, hi_e = ep.expert_range(rank, e_rank)
-        mine = sorted({int(g) for g in idx.ravel() if lo_e <= g < hi_e})
-        assert all(ep.owner_of(g, world, e_rank) == rank for g in mine)
+        placement = ([[g for g in range(world * e_rank) if g % world == d] for d in range(world)]
+                     if interleaved else None)
+        own = owner_map(world, e_rank, placement)
+        mine = sorted({int(g) for g in idx.ravel() if own.get(int(g)) == rank})
+        if not interleaved:
+            lo_e, hi_e = ep.expert_range(rank, e_rank)
+            assert all(lo_e <= g < hi_e and ep.owner_of(g, world, e_rank) == rank for g in mine)
         contrib = per_expert_outputs(pkg, oracle, cfg, mine)
         # Owner side: one fp32 partial per (token, this owner), for every global token.
-        partials = {t: owner_partial(contrib, idx, t, rank, world, e_rank) for t in range(T_global)}
+        partials = {t: owner_partial(contrib, idx, t, rank, world, e_rank, placement) for t in range(T_global)}
         gathered = [None] * world
         dist.all_gather_object(gathered, partials)
         # Source side: combine the own tokens' partials in ascending owner order.
@@ -106,11 +123,11 @@ def gloo_worker(rank: int, world: int, port: int, T_global: int, e_rank: int, se
         dist.all_gather_object(outs, out)
         if rank == 0:
             got = np.stack([r for o in outs for r in o])
-            allx = sorted({int(g) for g in idx.ravel() if g < world * e_rank})
+            allx = sorted({int(g) for g in idx.ravel() if int(g) in own})
             full = per_expert_outputs(pkg, oracle, cfg, allx)
             tokens = list(range(T_global))
-            np.testing.assert_array_equal(got, ep_expected_bits(oracle, full, idx, tokens, world, e_rank))
-            ref = layer_oracle_bits(oracle, full, idx, tokens, world, e_rank)
+            np.testing.assert_array_equal(got, ep_expected_bits(oracle, full, idx, tokens, world, e_rank, placement))
+            ref = layer_oracle_bits(oracle, full, idx, tokens, world, e_rank, placement)
             r = oracle.check_tolerance(ref, got)
             assert r["bad"] == 0, r
     finally:

@@ -96,8 +96,10 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def test_two_rank_gloo_dataflow_matches_layer_oracle():
-    """Full 256-expert layer over 2 ranks (128 experts each), 4 tokens split 2 + 2."""
+@pytest.mark.parametrize("interleaved", [False, True], ids=["contiguous", "interleaved"])
+def test_two_rank_gloo_dataflow_matches_layer_oracle(interleaved):
+    """Full 256-expert layer over 2 ranks (128 experts each), 4 tokens split 2 + 2, with contiguous
+    expert ranges or an interleaved placement."""
     world = 2
-    mp.start_processes(ep_helpers.gloo_worker, args=(world, _free_port(), 4, 128, 0), nprocs=world,
+    mp.start_processes(ep_helpers.gloo_worker, args=(world, _free_port(), 4, 128, 0, interleaved), nprocs=world,
                        join=True, start_method="spawn")
