@@ -58,6 +58,9 @@ CUDA_SIGNATURES = {
                                         c_void_p, c_void_p, c_void_p, c_float, c_int, c_void_p,
                                         c_void_p, c_size_t, c_void_p, c_void_p]),
     "moe_quantize_hidden": (c_int, [c_void_p, c_int, c_void_p, c_void_p, c_void_p]),
+    "moe_gate_packed_bytes": (c_size_t, []),
+    "moe_pack_gate": (c_int, [c_void_p, c_void_p, c_void_p]),
+    "moe_gate_quantize": (c_int, [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_void_p]),
     "moe_synth_logits": (c_int, [c_void_p, c_uint64, c_int, c_int, c_void_p, c_void_p]),
     "moe_synth_bias": (c_int, [c_void_p, c_uint64, c_int, c_float, c_void_p, c_int, c_float,
                                c_void_p, c_void_p]),

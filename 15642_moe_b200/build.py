@@ -25,7 +25,7 @@ CUDA_LIB = os.path.join(PKG_DIR, "libmoe_b200.so")
 SYNTH_CPU_LIB = os.path.join(PKG_DIR, "libmoe_synth_cpu.so")
 
 CUDA_SOURCES = ["moe_b200.cu"]
-CUDA_HEADERS = ["moe_common.cuh", "route.cuh", "ep.cuh", "gemm1.cuh", "gemm2.cuh", "pack.cuh", "quant.cuh", "synth.cuh",
+CUDA_HEADERS = ["moe_common.cuh", "route.cuh", "ep.cuh", "gemm1.cuh", "gemm2.cuh", "pack.cuh", "quant.cuh", "gate.cuh", "synth.cuh",
                 "synth_core.h"]
 
 NVCC_FLAGS = [

@@ -20,8 +20,11 @@
 #include "gemm2.cuh"
 #include "pack.cuh"
 #include "quant.cuh"
+#include "gate.cuh"
 #include "synth.cuh"
 #include "moe_b200.h"
+
+#include <cudaTypedefs.h>
 
 #include <cstring>
 #include <mutex>
@@ -79,6 +82,10 @@ int device_info(DeviceInfo** out) {
                                                  cudaFuncAttributeMaxDynamicSharedMemorySize, G2_SMEM),
                             "cudaFuncSetAttribute(gemm2)"))
       return rc;
+    if (int rc = cuda_check(cudaFuncSetAttribute(gate_quantize_kernel,
+                                                 cudaFuncAttributeMaxDynamicSharedMemorySize, GATE_SMEM),
+                            "cudaFuncSetAttribute(gate)"))
+      return rc;
     // setmaxnreg.inc in the epilogue warpgroups only completes if the CTA was launched with
     // enough registers for the whole split; refuse to launch a build where it could stall.
     cudaFuncAttributes fa1{}, fa2{};
@@ -104,6 +111,37 @@ int noalloc_scratch(DeviceInfo* d, void** out) {
     d->noalloc_scratch = p;
   }
   *out = d->noalloc_scratch;
+  return MOE_OK;
+}
+
+// cuTensorMapEncodeTiled from the driver, looked up once through the runtime (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static std::once_flag once;
+  std::call_once(once, [] {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q{};
+    if (cudaGetDriverEntryPointByVersion("cuTensorMapEncodeTiled", &p, 12000, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  });
+  return fn;
+}
+
+// Tensor map of bf16 hidden [T, 7168] read as 128-row x 64-column boxes with the 128-byte
+// swizzle (the K-major operand layout of the MMA); rows past T read as zero.
+int hidden_bf16_map(const void* hidden, int T, CUtensorMap* map) {
+  PFN_cuTensorMapEncodeTiled_v12000 encode = tensor_map_encoder();
+  if (encode == nullptr) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled is not available from the driver");
+  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(H), static_cast<cuuint64_t>(T)};
+  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(H) * 2};
+  const cuuint32_t box[2] = {64, TILE_M};
+  const cuuint32_t elem[2] = {1, 1};
+  const CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(hidden), dims, strides,
+                            box, elem, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                            CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) return fail(MOE_ERR_CUDA, "cuTensorMapEncodeTiled failed with code " + std::to_string(r));
   return MOE_OK;
 }
 
@@ -467,6 +505,41 @@ int moe_quantize_hidden(const void* hidden_bf16, int T, void* out_e4m3, float* o
   quantize_hidden_kernel<<<grid_for(warps, 8, d->num_sms * 8), 256, 0, static_cast<cudaStream_t>(stream)>>>(
       static_cast<const uint16_t*>(hidden_bf16), T, static_cast<uint8_t*>(out_e4m3), out_scale);
   return cuda_check(cudaGetLastError(), "quantize_hidden launch");
+}
+
+size_t moe_gate_packed_bytes(void) { return GATE_PACKED_BYTES; }
+
+int moe_pack_gate(const void* w_gate_bf16, void* gate_packed, void* stream) {
+  if (!w_gate_bf16 || !gate_packed) return fail(MOE_ERR_INVALID, "moe_pack_gate: null pointer argument");
+  if (!aligned16(w_gate_bf16) || !aligned16(gate_packed))
+    return fail(MOE_ERR_INVALID, "moe_pack_gate: W_gate and the packed buffer must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  pack_gate_kernel<<<grid_for(static_cast<size_t>(E_GLOBAL) * H * 2 / 16, 256, d->num_sms * 8), 256, 0,
+                     static_cast<cudaStream_t>(stream)>>>(static_cast<const uint8_t*>(w_gate_bf16),
+                                                           static_cast<uint8_t*>(gate_packed));
+  return cuda_check(cudaGetLastError(), "pack_gate_kernel launch");
+}
+
+int moe_gate_quantize(const void* hidden_bf16, const void* gate_packed, int T, float* logits,
+                      void* out_e4m3, float* out_scale, void* stream) {
+  if (T < 0) return fail(MOE_ERR_INVALID, "moe_gate_quantize: hidden must be [T, 7168]");
+  if (T == 0) return MOE_OK;
+  if (T > MAX_TOKENS) return fail(MOE_ERR_INVALID, "moe_gate_quantize: T must be at most 65536");
+  if (!hidden_bf16 || !gate_packed || !logits || !out_e4m3 || !out_scale)
+    return fail(MOE_ERR_INVALID, "moe_gate_quantize: null pointer argument");
+  if (!aligned16(hidden_bf16) || !aligned16(gate_packed) || !aligned16(logits) || !aligned16(out_e4m3) ||
+      !aligned16(out_scale))
+    return fail(MOE_ERR_INVALID, "moe_gate_quantize: every tensor must be 16-byte aligned");
+  DeviceInfo* d = nullptr;
+  if (int rc = device_info(&d)) return rc;
+  CUtensorMap map;
+  if (int rc = hidden_bf16_map(hidden_bf16, T, &map)) return rc;
+  const GateArgs args{static_cast<const uint8_t*>(gate_packed), T, logits, static_cast<uint8_t*>(out_e4m3),
+                      out_scale};
+  const dim3 grid(GATE_KS, (T + TILE_M - 1) / TILE_M);
+  gate_quantize_kernel<<<grid, GATE_THREADS, GATE_SMEM, static_cast<cudaStream_t>(stream)>>>(map, args);
+  return cuda_check(cudaGetLastError(), "gate_quantize launch");
 }
 
 int moe_synth_logits(const float* table, uint64_t seed, int T, int E, float* out, void* stream) {

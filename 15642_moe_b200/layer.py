@@ -201,6 +201,56 @@ def quantize_hidden(hidden: torch.Tensor, out: torch.Tensor | None = None,
     return out, scale
 
 
+GATE_PACKED_SHAPE = (H_BLOCKS, 2, E_GLOBAL, 128)   # per 128-column block: two swizzled halves
+
+
+def pack_gate(w_gate: torch.Tensor) -> torch.Tensor:
+    """W_gate bf16 [256, 7168] (the DeepSeek-V3 router weight) -> packed uint8 images for
+    gate_quantize, once per weight set."""
+    _check(w_gate.dim() == 2 and tuple(w_gate.shape) == (E_GLOBAL, H), "W_gate must be [256, 7168]")
+    _check(w_gate.dtype == torch.bfloat16, "W_gate must be bfloat16")
+    _check(w_gate.is_contiguous(), "W_gate must be contiguous")
+    _cuda(w_gate, "W_gate")
+    lib = _native.cuda_lib()
+    out = torch.empty(int(lib.moe_gate_packed_bytes()), dtype=torch.uint8, device=w_gate.device)
+    with torch.cuda.device(w_gate.device):
+        _native.check(lib.moe_pack_gate(w_gate.data_ptr(), out.data_ptr(), _stream(w_gate.device)))
+    return out.view(GATE_PACKED_SHAPE)
+
+
+def gate_quantize(hidden: torch.Tensor, gate_packed: torch.Tensor, logits: torch.Tensor | None = None,
+                  out: torch.Tensor | None = None, scale: torch.Tensor | None = None):
+    """MoE prologue in one pass over bf16 hidden [T, 7168]: (routing logits fp32 [T, 256] =
+    hidden . W_gate^T, e4m3 codes [T, 7168], fp32 scales [56, T]). The codes and scales equal
+    quantize_hidden's; the three outputs are moe_forward's routing_logits, hidden_states and
+    hidden_states_scale."""
+    _check(hidden.dim() == 2 and int(hidden.size(1)) == H, "hidden must be [T, 7168]")
+    _check(hidden.dtype == torch.bfloat16, "hidden must be bfloat16")
+    _check(hidden.is_contiguous(), "hidden must be contiguous")
+    _cuda(hidden, "hidden")
+    _check(gate_packed.dtype == torch.uint8 and tuple(gate_packed.shape) == GATE_PACKED_SHAPE
+           and gate_packed.is_contiguous(), "gate_packed must come from pack_gate")
+    _check(gate_packed.device == hidden.device, "gate_packed must be on the device of hidden")
+    T, dev = int(hidden.size(0)), hidden.device
+    if logits is None:
+        logits = torch.empty((T, E_GLOBAL), dtype=torch.float32, device=dev)
+    if out is None:
+        out = torch.empty((T, H), dtype=torch.float8_e4m3fn, device=dev)
+    if scale is None:
+        scale = torch.empty((H_BLOCKS, T), dtype=torch.float32, device=dev)
+    _check(logits.dtype == torch.float32 and tuple(logits.shape) == (T, E_GLOBAL) and logits.is_contiguous(),
+           "logits must be a contiguous float32 [T, 256] tensor")
+    _check(out.element_size() == 1 and tuple(out.shape) == (T, H) and out.is_contiguous(),
+           "out must be a contiguous FP8 [T, 7168] tensor")
+    _check(scale.dtype == torch.float32 and tuple(scale.shape) == (H_BLOCKS, T) and scale.is_contiguous(),
+           "scale must be a contiguous float32 [56, T] tensor")
+    with torch.cuda.device(dev):
+        _native.check(_native.cuda_lib().moe_gate_quantize(hidden.data_ptr(), gate_packed.data_ptr(), T,
+                                                           logits.data_ptr(), out.data_ptr(), scale.data_ptr(),
+                                                           _stream(dev)))
+    return logits, out, scale
+
+
 def route(logits: torch.Tensor, bias: torch.Tensor, rsf: float):
     """(topk_idx int32 [T, 8], topk_w fp32 [T, 8]) from the device router."""
     _check(logits.dim() == 2 and logits.size(1) == E_GLOBAL and logits.dtype == torch.float32,

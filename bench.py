@@ -331,7 +331,16 @@ def bench_ours(args, rank, world, local_rank, dist):
         pkg.quantize_hidden(xq, qo, qs)
     q_ms = time_steps(lambda: pkg.quantize_hidden(xq, qo, qs), 20) / 20
     q_bytes = TQ * (7168 * 2 + 7168 + 56 * 4)
-    del xq, qo, qs
+    # Gate GEMM fused with the quantiser on the same rows: logits + codes + scales in one pass.
+    wg = (0.02 * torch.randn((256, 7168), device=device)).to(torch.bfloat16)
+    gp = pkg.pack_gate(wg)
+    gl = torch.empty((TQ, 256), dtype=torch.float32, device=device)
+    for _ in range(3):
+        pkg.gate_quantize(xq, gp, gl, qo, qs)
+    g_ms = time_steps(lambda: pkg.gate_quantize(xq, gp, gl, qo, qs), 20) / 20
+    g_bytes = q_bytes + TQ * 256 * 4 + 256 * 7168 * 2
+    g_flops = 2.0 * TQ * 256 * 7168
+    del xq, qo, qs, wg, gp, gl
 
     e2e = e2e_run(pkg, inp, device, args.steps, args.warmup)
     if dist is not None:
@@ -374,6 +383,12 @@ def bench_ours(args, rank, world, local_rank, dist):
                      "achieved_gbs": round(q_bytes / (q_ms * 1e-3) / 1e9, 1),
                      "hbm_frac": round(q_bytes / (q_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                      "kernel": "quantize_hidden_kernel: bf16 [T,7168] -> e4m3 + [56,T] scales"},
+        "gate_quantize": {"T": TQ, "us": round(g_ms * 1e3, 2), "bytes": g_bytes,
+                          "achieved_gbs": round(g_bytes / (g_ms * 1e-3) / 1e9, 1),
+                          "hbm_frac": round(g_bytes / (g_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                          "tflops": round(g_flops / (g_ms * 1e-3) / 1e12, 1),
+                          "kernel": "gate_quantize_kernel: bf16 [T,7168] -> fp32 logits [T,256] "
+                                    "(tcgen05 bf16) + e4m3 + [56,T] scales, one read of the rows"},
         "e2e": {"value": round(cfg.T * world / (e2e["ms_per_step"] * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
                 "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],

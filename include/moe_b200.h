@@ -159,6 +159,23 @@ int moe_workspace_layout(int T, int E_local, size_t* offsets, int n);
  * No reference counterpart: the reference receives already-quantised activations. */
 int moe_quantize_hidden(const void* hidden_bf16, int T, void* out_e4m3, float* out_scale, void* stream);
 
+/* ---- MoE prologue: gate (router) GEMM fused with the FP8 quantiser ----
+ * The DeepSeek-V3 gate computes the routing logits from the same normalised bf16 hidden rows
+ * that the experts consume quantised. moe_gate_quantize reads those rows once and writes both:
+ *   logits [T, 256] fp32 = hidden . W_gate^T (bf16 operands, fp32 accumulation; each token's
+ *                          logits are independent of T and of its position in the batch),
+ *   codes [T, 7168] e4m3 + scale [56, T] fp32, bit-identical to moe_quantize_hidden.
+ * Together they are the routing_logits / hidden_states / hidden_states_scale inputs of
+ * moe_forward (reference/moe_ref.py:5-16). No reference counterpart: the reference receives
+ * logits and quantised activations as inputs.
+ *
+ * moe_pack_gate: W_gate bf16 [256, 7168] -> moe_gate_packed_bytes() bytes of packed images,
+ * once per weight set. */
+size_t moe_gate_packed_bytes(void);
+int moe_pack_gate(const void* w_gate_bf16, void* gate_packed, void* stream);
+int moe_gate_quantize(const void* hidden_bf16, const void* gate_packed, int T, float* logits,
+                      void* out_e4m3, float* out_scale, void* stream);
+
 /* ---- Seeded synthetic inputs on the GPU (bit-identical to the CPU generator) ----
  * table: device fp32 [65537] inverse-normal-CDF table (see the Python package).
  * No reference counterpart: the reference draws inputs with torch (moe_layer.py:47-74). */

@@ -137,6 +137,24 @@ def quantize_hidden(x: np.ndarray):
     return codes.reshape(T, H), np.ascontiguousarray(scale.T)
 
 
+# ---------------------------------------------------------------------------- gate (router) GEMM
+def gate_logits(x: np.ndarray, w_gate: np.ndarray):
+    """Routing logits of the DeepSeek-V3 gate, logits = x . W_gate^T over the fp32-upcast bf16
+    operands (transformers' DeepseekV3TopkRouter.forward, models/deepseek_v3/
+    modeling_deepseek_v3.py:150, F.linear in float32). Returns (fp64 logits, fp64 sum_k |x w|):
+    the exact dot products (every bf16 product is exact and fp64 holds the sums of 7168 of them
+    to about 2^-40 relative), and the scale against which an fp32 accumulation's error is bounded.
+    Test infrastructure: the reference receives the logits as an input."""
+    x64 = np.asarray(x, np.float64)
+    w64 = np.asarray(w_gate, np.float64)
+    return x64 @ w64.T, np.abs(x64) @ np.abs(w64).T
+
+
+def bf16_bits_to_f32(u: np.ndarray) -> np.ndarray:
+    """bf16 bit patterns (uint16) -> the fp32 values they represent."""
+    return (np.asarray(u, np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
 # ---------------------------------------------------------------------------- expert compute
 def dequant_hidden(hidden_u8: np.ndarray, hidden_scale: np.ndarray) -> np.ndarray:
     """A = fp8(hidden) * scale[h/128, t] (moe_ref.py:59-67)."""
