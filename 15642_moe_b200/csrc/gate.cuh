@@ -200,12 +200,53 @@ __device__ __forceinline__ bool block_scale(uint32_t mx, const GateCtrl* ctl, fl
   return false;
 }
 
+struct Words16 {
+  uint32_t v[16];
+};
+struct Codes8 {
+  uint32_t v[8];
+};
+
+// e4m3 codes (with the signs OR-ed in) of 8 consecutive values from their quotients q by the
+// block scale: two cvt.rn.satfinite.e4m3x2 per 4 values.
+__device__ __forceinline__ uint32_t codes4(float2 q0, float2 q1, uint32_t w0, uint32_t w1) {
+  const uint32_t c0 = __nv_cvt_float2_to_fp8x2(q0, __NV_SATFINITE, __NV_E4M3);
+  const uint32_t c1 = __nv_cvt_float2_to_fp8x2(q1, __NV_SATFINITE, __NV_E4M3);
+  return (c0 | (c1 << 16)) | (__byte_perm(w0, w1, 0x7531) & 0x80808080u);
+}
+
+// Blocks whose amax is below 2^-80 (rare): IEEE division per value. Out of line and by value,
+// so its code stays out of the quantiser's loop and the fast path keeps its operands in registers.
+__device__ __noinline__ Codes8 quantise32_divide(Words16 w, float s) {
+  Codes8 out;
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    float2 q[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const uint32_t u = w.v[2 * k + h];
+      q[h] = make_float2(__fdiv_rn(__uint_as_float(u << 16), s), __fdiv_rn(__uint_as_float(u & 0xFFFF0000u), s));
+    }
+    out.v[k] = codes4(q[0], q[1], w.v[2 * k], w.v[2 * k + 1]);
+  }
+  return out;
+}
+
 // Quantise 32 bf16 values (16 words, two values per word, low half first) that share the block
 // scale s (y = RN(1/s) when `fast`): returns 8 words of e4m3 codes in the same order. The sign
 // of x is OR-ed into each code so that -0 codes as 0x80 (e4m3 is sign-magnitude; every other
 // value already carries its sign through the quotient).
 __device__ __forceinline__ void quantise32(const uint32_t (&w)[16], float s, float y, bool fast,
                                            uint32_t (&out)[8]) {
+  if (!fast) {
+    Words16 ww;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) ww.v[i] = w[i];
+    const Codes8 c = quantise32_divide(ww, s);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) out[i] = c.v[i];
+    return;
+  }
   const uint64_t yy = f2_pack(y, y), ns = f2_pack(-s, -s);
 #pragma unroll
   for (int k = 0; k < 8; ++k) {
@@ -213,21 +254,13 @@ __device__ __forceinline__ void quantise32(const uint32_t (&w)[16], float s, flo
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const uint32_t u = w[2 * k + h];
-      const float lo = __uint_as_float(u << 16), hi = __uint_as_float(u & 0xFFFF0000u);
-      if (fast) {
-        const uint64_t x = f2_pack(lo, hi);
-        uint64_t t = f2_mul(x, yy);
-        t = f2_fma(f2_fma(t, ns, x), yy, t);
-        t = f2_fma(f2_fma(t, ns, x), yy, t);
-        q[h] = f2_unpack(t);
-      } else {
-        q[h] = make_float2(__fdiv_rn(lo, s), __fdiv_rn(hi, s));
-      }
+      const uint64_t x = f2_pack(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
+      uint64_t t = f2_mul(x, yy);
+      t = f2_fma(f2_fma(t, ns, x), yy, t);
+      t = f2_fma(f2_fma(t, ns, x), yy, t);
+      q[h] = f2_unpack(t);
     }
-    const uint32_t c0 = __nv_cvt_float2_to_fp8x2(q[0], __NV_SATFINITE, __NV_E4M3);
-    const uint32_t c1 = __nv_cvt_float2_to_fp8x2(q[1], __NV_SATFINITE, __NV_E4M3);
-    const uint32_t signs = __byte_perm(w[2 * k], w[2 * k + 1], 0x7531) & 0x80808080u;
-    out[k] = (c0 | (c1 << 16)) | signs;
+    out[k] = codes4(q[0], q[1], w[2 * k], w[2 * k + 1]);
   }
 }
 
