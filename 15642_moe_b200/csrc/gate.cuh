@@ -31,17 +31,15 @@
  *
  * Quantisation is the convention of the benchmark configurations (bit-identical to
  * quantize_hidden_kernel): scale = amax / 448 (IEEE division, 1 for an all-zero block),
- * code = e4m3(x / scale) rounded to nearest even, saturated to +-448. x / scale is formed from
- * y = RN(1 / scale) by Markstein's method (P. Markstein, "Computation of elementary functions on
- * the IBM RISC System/6000 processor", IBM J. Res. Dev. 34(1), 1990): q1 = RN(x y), then twice
- * r = x - scale q (exact with an FMA) and q = RN(q + r y). The first correction brings q within
- * one ulp of x / scale and the second then returns the correctly rounded quotient, so the codes
- * equal those of a true division. The block scale and y come from 128-entry tables indexed by
- * the amax mantissa (see block_scale). Blocks whose amax is below 2^-80 (where the remainder
- * could underflow) divide directly.
+ * code = e4m3(x / scale) rounded to nearest even, saturated to +-448. x / scale is the correctly
+ * rounded quotient from y = RN(1 / scale) by Markstein's method with two corrections (quotient2 in
+ * quant.cuh), so the codes equal those of a true division. The block scale and y come from
+ * 128-entry tables indexed by the amax mantissa (see block_scale). Blocks whose amax is below
+ * 2^-80 (where the remainder could underflow) divide directly, out of line.
  */
 #pragma once
 #include "moe_common.cuh"
+#include "quant.cuh"
 
 #include <cuda.h>
 
@@ -161,27 +159,6 @@ __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
   return v;
 }
 
-__device__ __forceinline__ uint64_t f2_pack(float a, float b) {
-  uint64_t r;
-  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
-  return r;
-}
-__device__ __forceinline__ float2 f2_unpack(uint64_t v) {
-  float2 r;
-  asm("mov.b64 {%0, %1}, %2;" : "=f"(r.x), "=f"(r.y) : "l"(v));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_mul(uint64_t a, uint64_t b) {
-  uint64_t r;
-  asm("mul.rn.f32x2 %0, %1, %2;" : "=l"(r) : "l"(a), "l"(b));
-  return r;
-}
-__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
-  uint64_t r;
-  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(r) : "l"(a), "l"(b), "l"(c));
-  return r;
-}
-
 // Block scale and its reciprocal from the bf16 bit pattern `mx` of the block's amax (sign
 // cleared). For amax = (1 + f/128) 2^(E-127) with E >= 47, s = RN(amax / 448) and y = RN(1 / s)
 // are the table entries for f scaled by 2^(E-127): scaling by a power of two commutes with
@@ -206,14 +183,6 @@ struct Words16 {
 struct Codes8 {
   uint32_t v[8];
 };
-
-// e4m3 codes (with the signs OR-ed in) of 8 consecutive values from their quotients q by the
-// block scale: two cvt.rn.satfinite.e4m3x2 per 4 values.
-__device__ __forceinline__ uint32_t codes4(float2 q0, float2 q1, uint32_t w0, uint32_t w1) {
-  const uint32_t c0 = __nv_cvt_float2_to_fp8x2(q0, __NV_SATFINITE, __NV_E4M3);
-  const uint32_t c1 = __nv_cvt_float2_to_fp8x2(q1, __NV_SATFINITE, __NV_E4M3);
-  return (c0 | (c1 << 16)) | (__byte_perm(w0, w1, 0x7531) & 0x80808080u);
-}
 
 // Blocks whose amax is below 2^-80 (rare): IEEE division per value. Out of line and by value,
 // so its code stays out of the quantiser's loop and the fast path keeps its operands in registers.
@@ -252,14 +221,7 @@ __device__ __forceinline__ void quantise32(const uint32_t (&w)[16], float s, flo
   for (int k = 0; k < 8; ++k) {
     float2 q[2];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const uint32_t u = w[2 * k + h];
-      const uint64_t x = f2_pack(__uint_as_float(u << 16), __uint_as_float(u & 0xFFFF0000u));
-      uint64_t t = f2_mul(x, yy);
-      t = f2_fma(f2_fma(t, ns, x), yy, t);
-      t = f2_fma(f2_fma(t, ns, x), yy, t);
-      q[h] = f2_unpack(t);
-    }
+    for (int h = 0; h < 2; ++h) q[h] = quotient2(bf16x2_to_f2(w[2 * k + h]), yy, ns);
     out[k] = codes4(q[0], q[1], w[2 * k], w[2 * k + 1]);
   }
 }

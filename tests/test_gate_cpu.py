@@ -1,7 +1,8 @@
-"""CPU checks of the fused gate + quantiser (csrc/gate.cuh) that need no GPU: the division it
-uses (Markstein's method with two corrections) restated over exact rationals and compared with
-the correctly rounded quotient, the router-GEMM restatement against torch's fp32 linear, and
-the C ABI's argument checks."""
+"""CPU checks of the quantisers (csrc/quant.cuh quotient2, used by quantize_hidden_kernel and
+gate_quantize_kernel) and of the fused gate kernel (csrc/gate.cuh) that need no GPU: the
+division (Markstein's method with two corrections) restated over exact rationals and compared
+with the correctly rounded quotient, the scale tables against direct division, the router-GEMM
+restatement against torch's fp32 linear, and the C ABI's argument checks."""
 import importlib
 from fractions import Fraction
 
