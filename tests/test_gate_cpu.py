@@ -87,6 +87,13 @@ def test_gate_capi_argument_errors(pkg):
     assert b"null" in lib.moe_last_error()
     assert lib.moe_pack_gate(None, None, None) == 1
     assert b"null" in lib.moe_last_error()
+    # Misaligned (non-null) pointers are refused on the host, before any device work.
+    odd, ok = 0x1008, 0x2000
+    assert lib.moe_gate_quantize(odd, ok, 4, ok, ok, ok, None) == 1
+    assert b"16-byte aligned" in lib.moe_last_error()
+    assert lib.moe_gate_quantize(ok, ok, 4, ok, ok, odd, None) == 1
+    assert lib.moe_pack_gate(ok, odd, None) == 1
+    assert b"16-byte aligned" in lib.moe_last_error()
 
 
 def test_scale_tables_equal_direct_division_for_every_fast_exponent():
