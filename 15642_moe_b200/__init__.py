@@ -14,6 +14,7 @@ Public surface (mirrors the reference's Python API):
   make_inputs(cfg, device)       seeded synthetic inputs of the benchmark configurations
   ExpertParallel                 expert-parallel layer over the GPUs of one node (ep.py)
   save_packed / load_packed      packed weights on disk (packed_io.py)
+  HostPipeline                   serving loop from/to pinned host memory on three streams (pipeline.py)
 """
 from .layer import (_cached_pack, _load_custom_ops, gate_quantize, moe_forward, ops, pack_gate, pack_w13,
                     pack_w2, quantize_hidden, route, run, run_custom, shared_expert_forward, workspace_bytes)
@@ -21,11 +22,12 @@ from .synth import CONFIGS, MoEConfig, make_inputs, make_weights, quantile_table
 from ._native import MoEError, device_status, workspace_layout
 from .ep import ExpertParallel, balanced_placement, expert_range, owner_of, token_range
 from .packed_io import load_packed, save_packed
+from .pipeline import HostPipeline
 
 __all__ = [
     "run", "run_custom", "ops", "pack_w13", "pack_w2", "moe_forward", "route", "workspace_bytes",
     "quantize_hidden", "shared_expert_forward", "pack_gate", "gate_quantize",
     "make_inputs", "make_weights", "MoEConfig", "CONFIGS", "quantile_table", "MoEError", "device_status",
     "workspace_layout", "_cached_pack", "_load_custom_ops", "ExpertParallel", "expert_range",
-    "owner_of", "token_range", "balanced_placement", "save_packed", "load_packed",
+    "owner_of", "token_range", "balanced_placement", "save_packed", "load_packed", "HostPipeline",
 ]

@@ -226,29 +226,39 @@ def load_traffic(workload: str) -> dict | None:
         return json.load(f).get(workload)
 
 
-def e2e_run(pkg, inp, device, steps: int, warmup: int, call=None) -> dict:
-    """Public API (pkg.run, or `call` with the same keywords) per step: H2D of the step's
-    activations from pinned host memory, the forward with resident weights, D2H of the bf16
-    result."""
-    call = pkg.run if call is None else call
-    host = {k: inp[k].cpu().pin_memory() for k in ("hidden_states", "hidden_states_scale", "routing_logits")}
-    dev = {k: torch.empty_like(inp[k]) for k in host}
-    out_host = torch.empty((inp["hidden_states"].shape[0], 7168), dtype=torch.bfloat16).pin_memory()
-    kw = dict(inp)
-
-    def one():
-        for k in host:
-            dev[k].copy_(host[k], non_blocking=True)
-        kw.update(dev)
-        out = call(**kw)
-        out_host.copy_(out, non_blocking=True)
-
-    for _ in range(warmup):
-        one()
-    ms = time_steps(one, steps)
-    h2d = sum(t.numel() * t.element_size() for t in host.values())
-    return {"ms_per_step": ms / steps, "h2d_bytes_per_step": int(h2d),
-            "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size())}
+def e2e_run(pkg, inp, device, steps: int, warmup: int, forward=None) -> dict:
+    """End to end through the public serving API (pkg.HostPipeline): every step copies its
+    activations in from pinned host memory, runs the layer with resident packed weights and
+    copies its bf16 result back to pinned host memory; neighbouring steps' copies overlap the
+    forward on separate streams. `forward(h, s, logits, out)` replaces the single-GPU layer (the
+    expert-parallel bench passes its context's forward). Timed with CUDA events from before the
+    first copy in to after the last copy out."""
+    T = int(inp["hidden_states"].shape[0])
+    if forward is None:
+        pipe = pkg.HostPipeline.for_layer(
+            pkg.pack_w13(inp["gemm1_weights"]), inp["gemm1_weights_scale"].float().contiguous(),
+            pkg.pack_w2(inp["gemm2_weights"]), inp["gemm2_weights_scale"].float().contiguous(),
+            inp["routing_bias"], float(inp["routed_scaling_factor"]), int(inp["local_expert_offset"]), T)
+    else:
+        pipe = pkg.HostPipeline(forward, T, device)
+    hidden = inp["hidden_states"].cpu().pin_memory()
+    scale = inp["hidden_states_scale"].float().cpu().pin_memory()
+    logits = inp["routing_logits"].float().cpu().pin_memory()
+    out_host = torch.empty((T, 7168), dtype=torch.bfloat16).pin_memory()
+    for _ in range(max(warmup, 3)):
+        pipe.submit(hidden, scale, logits, out_host)
+    pipe.synchronize()
+    torch.cuda.synchronize()
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record(pipe.h2d_stream)
+    for _ in range(steps):
+        pipe.submit(hidden, scale, logits, out_host)
+    end.record(pipe.d2h_stream)
+    torch.cuda.synchronize()
+    h2d = sum(t.numel() * t.element_size() for t in (hidden, scale, logits))
+    return {"ms_per_step": start.elapsed_time(end) / steps, "h2d_bytes_per_step": int(h2d),
+            "d2h_bytes_per_step": int(out_host.numel() * out_host.element_size()),
+            "api": "HostPipeline (3 streams, double-buffered device slots)"}
 
 
 def cpu_oracle_time(pkg, inp, max_seconds: float, experts=None) -> tuple[float, str, int]:
@@ -392,7 +402,7 @@ def bench_ours(args, rank, world, local_rank, dist):
         "e2e": {"value": round(cfg.T * world / (e2e["ms_per_step"] * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
                 "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
-                "ms_per_step": round(e2e["ms_per_step"], 4)},
+                "ms_per_step": round(e2e["ms_per_step"], 4), "api": e2e["api"]},
         "gpu_launches": len(STAGES) * args.steps,
         "clocks": clocks,
         "device_status": status,
@@ -509,8 +519,17 @@ def bench_ep(args, rank, world, local_rank, dist):
         dist.all_gather(parts, mine_t)
         per_rank = [p.tolist() for p in parts]
 
-        kw = {kk: v for kk, v in mine.items() if kk != "local_expert_offset"}
-        e2e = e2e_run(pkg, kw, device, args.steps, args.warmup, call=ctx.run)
+        w13p_e, w2p_e = pkg.pack_w13(mine["gemm1_weights"]), pkg.pack_w2(mine["gemm2_weights"])
+        s13_e = mine["gemm1_weights_scale"].float().contiguous()
+        s2_e = mine["gemm2_weights_scale"].float().contiguous()
+        bias_e = mine["routing_bias"].float().reshape(-1).contiguous()
+        rsf_e = float(mine["routed_scaling_factor"])
+
+        def ep_layer(h, sc, lg, out):
+            ctx.forward(h, sc, w13p_e, s13_e, w2p_e, s2_e, lg, bias_e, rsf_e, out=out)
+
+        dist.barrier()
+        e2e = e2e_run(pkg, mine, device, args.steps, args.warmup, forward=ep_layer)
         t = torch.tensor([e2e["ms_per_step"]], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e["ms_per_step"] = float(t.item())
@@ -556,7 +575,8 @@ def bench_ep(args, rank, world, local_rank, dist):
         "e2e": {"value": round(slices / (e2e["ms_per_step"] * 1e-3), 1), "unit": "tokens/s",
                 "h2d_bytes_per_step": e2e["h2d_bytes_per_step"],
                 "d2h_bytes_per_step": e2e["d2h_bytes_per_step"],
-                "ms_per_step": round(e2e["ms_per_step"], 4), "per": "rank 0 (max over ranks)"},
+                "ms_per_step": round(e2e["ms_per_step"], 4), "per": "rank 0 (max over ranks)",
+                "api": e2e["api"]},
         "gpu_launches": 10 * args.steps,
         "clocks": clocks,
         "device_status": status,
