@@ -519,14 +519,8 @@ def bench_ep(args, rank, world, local_rank, dist):
         dist.all_gather(parts, mine_t)
         per_rank = [p.tolist() for p in parts]
 
-        w13p_e, w2p_e = pkg.pack_w13(mine["gemm1_weights"]), pkg.pack_w2(mine["gemm2_weights"])
-        s13_e = mine["gemm1_weights_scale"].float().contiguous()
-        s2_e = mine["gemm2_weights_scale"].float().contiguous()
-        bias_e = mine["routing_bias"].float().reshape(-1).contiguous()
-        rsf_e = float(mine["routed_scaling_factor"])
-
-        def ep_layer(h, sc, lg, out):
-            ctx.forward(h, sc, w13p_e, s13_e, w2p_e, s2_e, lg, bias_e, rsf_e, out=out)
+        def ep_layer(h, sc, lg, o):       # the same layer as `step`, on the pipeline's buffers
+            ctx.forward(h, sc, w13p, k["s13"], w2p, k["s2"], lg, k["b"], float(cfg.routed_scaling_factor), out=o)
 
         dist.barrier()
         e2e = e2e_run(pkg, mine, device, args.steps, args.warmup, forward=ep_layer)
