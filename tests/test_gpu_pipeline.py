@@ -60,3 +60,34 @@ def test_pipeline_argument_checks(pkg):
         pipe.submit(h, sc, torch.zeros((5, 256)).pin_memory(), o)
     pipe.submit(h, sc, lg, o)
     pipe.synchronize()
+
+
+def test_pipeline_with_expert_parallel_forward(pkg):
+    """The pipeline around an expert-parallel context (single rank: dispatch, flag barriers,
+    owner-side and final combine on one GPU) on the pipeline's compute stream returns, for every
+    step, moe_forward's output on that step's inputs."""
+    cfg = pkg.CONFIGS[1].with_(T=40)
+    base = pkg.make_inputs(cfg, "cuda")
+    w13p, w2p = pkg.pack_w13(base["gemm1_weights"]), pkg.pack_w2(base["gemm2_weights"])
+    s13 = base["gemm1_weights_scale"].float().contiguous()
+    s2 = base["gemm2_weights_scale"].float().contiguous()
+    bias = base["routing_bias"].float().reshape(-1).contiguous()
+    rsf = float(base["routed_scaling_factor"])
+    steps = _step_inputs(base, 4)
+    with pkg.ExpertParallel(t_rank_max=cfg.T, e_rank=32) as ep:
+        def layer(h, sc, lg, o):
+            ep.forward(h, sc, w13p, s13, w2p, s2, lg, bias, rsf, out=o)
+
+        pipe = pkg.HostPipeline(layer, cfg.T, depth=2)
+        outs = []
+        for inp in steps:
+            o = torch.empty((cfg.T, 7168), dtype=torch.bfloat16).pin_memory()
+            pipe.submit(inp["hidden_states"].cpu().pin_memory(), inp["hidden_states_scale"].cpu().pin_memory(),
+                        inp["routing_logits"].cpu().pin_memory(), o)
+            outs.append(o)
+        pipe.synchronize()
+    assert pkg.device_status(reset=True) == 0
+    for inp, got in zip(steps, outs):
+        ref = pkg.moe_forward(inp["hidden_states"], inp["hidden_states_scale"], w13p, s13, w2p, s2,
+                              inp["routing_logits"], bias, rsf, 0)
+        assert torch.equal(got.view(torch.int16), ref.cpu().view(torch.int16))
