@@ -629,6 +629,11 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)
+    # Standard output carries the one JSON line only: keep a handle on it, then send whatever
+    # else writes to file descriptor 1 (NCCL's version banner, library prints) to stderr.
+    sys.stdout.flush()
+    result_out = os.fdopen(os.dup(1), "w")
+    os.dup2(2, 1)
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
@@ -636,7 +641,7 @@ def main():
     if args.impl == "reference":
         line = bench_reference(args, rank)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            print(json.dumps(line), file=result_out, flush=True)
         return
 
     dist = None
@@ -650,7 +655,7 @@ def main():
     try:
         line = (bench_ours if world == 1 else bench_ep)(args, rank, world, local_rank, dist)
         if line is not None:
-            print(json.dumps(line), flush=True)
+            print(json.dumps(line), file=result_out, flush=True)
     finally:
         if dist is not None:
             dist.barrier()
