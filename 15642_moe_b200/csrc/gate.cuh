@@ -24,10 +24,10 @@
  *               MMA reads, release it, and write the e4m3 codes and the block scale; after the
  *               last block they copy the accumulator to shared memory
  * The x ring is the deep one: it keeps 4 blocks (128 KB) of HBM reads in flight per SM, and the
- * MMA's time on a block is not on the path that refills it.
- * then the cluster sums its GATE_KS partial accumulators through distributed shared memory in
- * K-slice order (CTA q reduces rows [32q, 32q + 32)), so every token's logits are computed the
- * same way whatever T is and wherever the token sits in the batch.
+ * MMA's time on a block is not on the path that refills it. After the last block the cluster
+ * sums its GATE_KS partial accumulators through distributed shared memory in K-slice order (CTA q
+ * reduces rows [32q, 32q + 32)), so every token's logits are computed the same way whatever T is
+ * and wherever the token sits in the batch.
  *
  * Quantisation is the convention of the benchmark configurations (bit-identical to
  * quantize_hidden_kernel): scale = amax / 448 (IEEE division, 1 for an all-zero block),
