@@ -19,7 +19,7 @@ Public surface (mirrors the reference's Python API):
 from .layer import (_cached_pack, _load_custom_ops, gate_quantize, moe_forward, ops, pack_gate, pack_w13,
                     pack_w2, quantize_hidden, route, run, run_custom, shared_expert_forward, workspace_bytes)
 from .synth import CONFIGS, MoEConfig, make_inputs, make_weights, quantile_table
-from ._native import MoEError, device_status, workspace_layout
+from ._native import MoEError, device_status, set_wait_limit_ns, wait_limit_ns, workspace_layout
 from .ep import ExpertParallel, balanced_placement, expert_range, owner_of, token_range
 from .packed_io import load_packed, save_packed
 from .pipeline import HostPipeline
@@ -27,7 +27,7 @@ from .pipeline import HostPipeline
 __all__ = [
     "run", "run_custom", "ops", "pack_w13", "pack_w2", "moe_forward", "route", "workspace_bytes",
     "quantize_hidden", "shared_expert_forward", "pack_gate", "gate_quantize",
-    "make_inputs", "make_weights", "MoEConfig", "CONFIGS", "quantile_table", "MoEError", "device_status",
+    "make_inputs", "make_weights", "MoEConfig", "CONFIGS", "quantile_table", "MoEError", "device_status", "set_wait_limit_ns", "wait_limit_ns",
     "workspace_layout", "_cached_pack", "_load_custom_ops", "ExpertParallel", "expert_range",
     "owner_of", "token_range", "balanced_placement", "save_packed", "load_packed", "HostPipeline",
 ]

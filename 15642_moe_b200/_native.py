@@ -24,6 +24,10 @@ c_size_t_p = ctypes.POINTER(ctypes.c_size_t)
 CUDA_SIGNATURES = {
     "moe_last_error": (ctypes.c_char_p, []),
     "moe_get_status": (c_int, [c_int_p, c_int]),
+    "moe_set_wait_limit_ns": (c_int, [ctypes.c_ulonglong]),
+    "moe_get_wait_limit_ns": (c_int, [ctypes.POINTER(ctypes.c_ulonglong)]),
+    "moe_probe_ep_barrier_timeout": (c_int, [c_void_p, c_void_p]),
+    "moe_probe_mbar_timeout": (c_int, [c_int, c_void_p, c_void_p]),
     "moe_pack_w13_bytes": (c_size_t, [c_int]),
     "moe_pack_w13": (c_int, [c_void_p, c_int, c_void_p, c_void_p]),
     "moe_pack_w2_bytes": (c_size_t, [c_int]),
@@ -131,6 +135,17 @@ def device_status(reset: bool = True) -> int:
     """Synchronise and return the kernels' status word (0 = no timeout / bad metadata)."""
     v = ctypes.c_int(0)
     check(cuda_lib().moe_get_status(ctypes.byref(v), 1 if reset else 0))
+    return v.value
+
+
+def set_wait_limit_ns(ns: int) -> None:
+    """Limit of every bounded wait in the kernels on the current device (default 2 s)."""
+    check(cuda_lib().moe_set_wait_limit_ns(int(ns)))
+
+
+def wait_limit_ns() -> int:
+    v = ctypes.c_ulonglong(0)
+    check(cuda_lib().moe_get_wait_limit_ns(ctypes.byref(v)))
     return v.value
 
 

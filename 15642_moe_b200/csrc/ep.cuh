@@ -34,8 +34,12 @@
  * writes epoch e + 1's comb rows only after every source signalled `arrive` for e + 1, which
  * each source does after its final combine of epoch e.
  *
- * Waits are bounded (WAIT_LIMIT_NS); on timeout the barrier reports ST_EP_TIMEOUT and
- * returns, and every consumer of peer-written metadata checks it before addressing memory.
+ * Waits are bounded (the device wait limit, 2 s by default); on timeout the barrier reports
+ * ST_EP_TIMEOUT and returns. Every consumer of peer-written metadata bounds-checks it before
+ * addressing memory, so a timed-out forward never reads or writes out of range; once the status
+ * word holds ST_EP_TIMEOUT the combine kernels stop exchanging data and the final combine writes
+ * NaN rows, so a forward that ran into a timeout cannot return plausible-looking numbers. The
+ * host learns of it through moe_get_status (ExpertParallel.forward(check=True) raises).
  * No load here uses TMA multicast; peers are read and written with plain loads and stores.
  */
 #pragma once
@@ -258,9 +262,9 @@ __global__ void __launch_bounds__(32) ep_barrier_kernel(const __grid_constant__ 
     __threadfence_system();
     st_release_sys(ep_at<unsigned>(peers.base[lane], flag_off) + rank, epoch);
     const unsigned* f = ep_at<unsigned>(peers.base[rank], flag_off) + lane;
-    const unsigned long long t0 = globaltimer();
+    const unsigned long long t0 = globaltimer(), limit = wait_limit_ns();
     while (static_cast<int>(ld_acquire_sys(f) - epoch) < 0) {
-      if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+      if (globaltimer() - t0 > limit) {
         report_status(ST_EP_TIMEOUT);
         break;
       }
@@ -282,6 +286,7 @@ __global__ void __launch_bounds__(COMBINE_THREADS) ep_combine_send_kernel(const 
   const int* tok_nr = ep_at<int>(me, L.tok_nr);
   const int* tok_route = ep_at<int>(me, L.tok_route);
   const int tid = threadIdx.x;
+  if (status_now() & ST_EP_TIMEOUT) return;   // a peer is missing: send nothing this epoch
   for (int i = blockIdx.x; i < L.r_cap; i += gridDim.x) {
     const int src = i / L.t_max, t = i - src * L.t_max;
     int tn = src_T[src];
@@ -324,6 +329,13 @@ __global__ void __launch_bounds__(COMBINE_THREADS) ep_final_combine_kernel(const
                                                                            __nv_bfloat16* __restrict__ out) {
   const int t = blockIdx.x;
   if (t >= T) return;
+  const int tid = threadIdx.x;
+  if (status_now() & ST_EP_TIMEOUT) {       // the exchange did not complete: NaN, not stale data
+    uint2* d = reinterpret_cast<uint2*>(out + static_cast<size_t>(t) * H) + tid;
+#pragma unroll
+    for (int j = 0; j < COMBINE_Q; ++j) d[j * COMBINE_THREADS] = make_uint2(0x7FC07FC0u, 0x7FC07FC0u);
+    return;
+  }
   const int* place = reinterpret_cast<const int*>(me + L.place);
   unsigned mask = 0;
 #pragma unroll
@@ -332,7 +344,6 @@ __global__ void __launch_bounds__(COMBINE_THREADS) ep_final_combine_kernel(const
     ep_owner(place, L, topk_idx[static_cast<size_t>(t) * TOP_K + k], d, le);
     if (d >= 0) mask |= 1u << d;
   }
-  const int tid = threadIdx.x;
   const float* comb = reinterpret_cast<const float*>(me + L.comb);
   float acc[16];
 #pragma unroll
@@ -340,6 +351,33 @@ __global__ void __launch_bounds__(COMBINE_THREADS) ep_final_combine_kernel(const
   for (int d = 0; d < L.world; ++d)
     if (mask & (1u << d)) add_row_f32(acc, comb + (static_cast<size_t>(d) * L.t_max + t) * H, tid);
   store_row_bf16(out + static_cast<size_t>(t) * H, acc, tid);
+}
+
+// Failure-path probe of ep_barrier_kernel on one GPU: the barrier of a 2-rank layout whose
+// second rank never exists. `buf` (>= 256 zeroed bytes) stands for both ranks' buffers: the epoch
+// lives at offset 0 and the flags at offset 64, so rank 0's own flag is set and the wait for
+// rank 1's runs out after the wait limit, reporting ST_EP_TIMEOUT.
+inline void launch_ep_barrier_probe(uint8_t* buf, cudaStream_t st) {
+  EpPeers peers{};
+  for (int d = 0; d < EP_MAX_RANKS; ++d) peers.base[d] = buf;
+  ep_barrier_kernel<<<1, 32, 0, st>>>(peers, 64, 0, 0, 2, 1);
+}
+
+// Failure-path probe of mbar_wait: one thread waits on an mbarrier nothing arrives on; after the
+// wait limit it raises the abort flag and reports `who`.
+__global__ void __launch_bounds__(32) mbar_probe_kernel(int who, int* aborted) {
+  __shared__ uint64_t bar;
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    mbar_init(&bar, 1);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncwarp();
+  if (threadIdx.x == 0) {
+    const bool ok = mbar_wait(&bar, 0, &abort_flag, who);
+    *aborted = ok ? 0 : (abort_flag ? 1 : 2);
+  }
 }
 
 }  // namespace moe

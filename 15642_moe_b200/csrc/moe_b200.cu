@@ -171,6 +171,31 @@ int moe_get_status(int* status, int reset) {
   return MOE_OK;
 }
 
+int moe_set_wait_limit_ns(unsigned long long ns) {
+  if (ns < 1000000ull || ns > 60000000000ull)
+    return fail(MOE_ERR_INVALID, "moe_set_wait_limit_ns: limit must be within [1 ms, 60 s]");
+  return cuda_check(cudaMemcpyToSymbol(g_wait_limit_ns, &ns, sizeof(ns)), "set wait limit");
+}
+
+int moe_get_wait_limit_ns(unsigned long long* ns) {
+  if (ns == nullptr) return fail(MOE_ERR_INVALID, "ns must not be null");
+  return cuda_check(cudaMemcpyFromSymbol(ns, g_wait_limit_ns, sizeof(*ns)), "read wait limit");
+}
+
+int moe_probe_ep_barrier_timeout(void* buf, void* stream) {
+  if (buf == nullptr || !aligned16(buf)) return fail(MOE_ERR_INVALID, "buf must be a 16-byte aligned device pointer");
+  launch_ep_barrier_probe(static_cast<uint8_t*>(buf), static_cast<cudaStream_t>(stream));
+  return cuda_check(cudaGetLastError(), "ep barrier probe launch");
+}
+
+int moe_probe_mbar_timeout(int who, int* aborted, void* stream) {
+  if (who != ST_TIMEOUT_PRODUCER && who != ST_TIMEOUT_MMA && who != ST_TIMEOUT_EPILOGUE)
+    return fail(MOE_ERR_INVALID, "who must be one of the role timeout bits 1, 2, 4");
+  if (aborted == nullptr) return fail(MOE_ERR_INVALID, "aborted must not be null");
+  mbar_probe_kernel<<<1, 32, 0, static_cast<cudaStream_t>(stream)>>>(who, aborted);
+  return cuda_check(cudaGetLastError(), "mbarrier probe launch");
+}
+
 size_t moe_pack_w13_bytes(int E_local) {
   return E_local > 0 ? static_cast<size_t>(E_local) * G1N * H : 0;
 }

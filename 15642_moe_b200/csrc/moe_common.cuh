@@ -41,11 +41,19 @@ constexpr int ST_TIMEOUT_EPILOGUE = 4;
 constexpr int ST_BAD_INDEX = 8;
 constexpr int ST_EP_TIMEOUT = 16;        // an expert-parallel barrier gave up waiting for a peer
 
-// A bounded wait gives up after this long and reports ST_TIMEOUT_*.
-constexpr unsigned long long WAIT_LIMIT_NS = 2000000000ull;  // 2 s
+// A bounded wait gives up after this long and reports ST_TIMEOUT_* / ST_EP_TIMEOUT. The limit
+// is a device variable (one per device) so a test can shorten it through moe_set_wait_limit_ns;
+// every wait reads it once when it starts.
+constexpr unsigned long long WAIT_LIMIT_DEFAULT_NS = 2000000000ull;  // 2 s
+__device__ unsigned long long g_wait_limit_ns = WAIT_LIMIT_DEFAULT_NS;
 
 // Device status word (one per device), read by moe_get_status().
 __device__ int g_status = 0;
+
+__device__ __forceinline__ unsigned long long wait_limit_ns() {
+  return *static_cast<volatile unsigned long long*>(&g_wait_limit_ns);
+}
+__device__ __forceinline__ int status_now() { return *static_cast<volatile int*>(&g_status); }
 
 // ------------------------------------------------------------------------------------------
 // Basic helpers
@@ -127,16 +135,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Bounded wait for the phase with the given parity to complete. Returns false when the
-// CTA-wide abort flag is raised or when WAIT_LIMIT_NS elapses (then it raises the flag and
+// CTA-wide abort flag is raised or when the wait limit elapses (then it raises the flag and
 // records `who` in g_status). Never spins forever.
 __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag,
                                           int who) {
   if (mbar_try_wait(bar, parity)) return true;
-  const unsigned long long t0 = globaltimer();
+  const unsigned long long t0 = globaltimer(), limit = wait_limit_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (globaltimer() - t0 > WAIT_LIMIT_NS) {
+    if (globaltimer() - t0 > limit) {
       *abort_flag = 1;
       report_status(who);
       return false;
@@ -147,9 +155,9 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volati
 // Bounded wait that ignores the abort flag: used on teardown to let in-flight async copies
 // and MMAs land before the CTA releases its shared memory and TMEM.
 __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) {
-  const unsigned long long t0 = globaltimer();
+  const unsigned long long t0 = globaltimer(), limit = wait_limit_ns();
   while (!mbar_try_wait(bar, parity)) {
-    if (globaltimer() - t0 > WAIT_LIMIT_NS) return false;
+    if (globaltimer() - t0 > limit) return false;
   }
   return true;
 }

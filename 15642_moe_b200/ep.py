@@ -171,9 +171,15 @@ class ExpertParallel:
         return list(self.placement[self.rank])
 
     def forward(self, hidden, hidden_scale, W13_packed, W13_scale, W2_packed, W2_scale, logits, bias,
-                rsf: float, out: torch.Tensor | None = None, events=None) -> torch.Tensor:
+                rsf: float, out: torch.Tensor | None = None, events=None, check: bool = False) -> torch.Tensor:
         """Layer output bf16 [T, 7168] for this rank's T tokens (moe_forward's argument order
-        without local_expert_offset: this rank's experts are implied by its rank)."""
+        without local_expert_offset: this rank's experts are implied by its rank).
+
+        The forward is asynchronous and never waits on the host. A peer that does not reach a
+        flag barrier within the device wait limit makes the barrier give up: the device status
+        word then holds ST_EP_TIMEOUT (16) and this forward's output rows are NaN. With
+        ``check=True`` the call synchronises, reads (and clears) the status word and raises
+        MoEError when any bit is set."""
         _check(self._ctx is not None, "expert-parallel context is closed")
         _check(hidden.dim() == 2 and int(hidden.size(1)) == H, "hidden must be [T, 7168]")
         T = int(hidden.size(0))
@@ -213,6 +219,11 @@ class ExpertParallel:
                 _check(len(events) == len(EP_EVENTS) + 1, "events must hold 10 CUDA events")
                 arr = (ctypes.c_void_p * len(events))(*[e.cuda_event for e in events])
                 _native.check(self.lib.moe_ep_forward_profiled(*args, arr))
+            if check:
+                status = _native.device_status(reset=True)
+                if status:
+                    raise _native.MoEError(f"expert-parallel forward reported device status {status} "
+                                           "(16 = a peer did not reach a barrier in time)")
         return out
 
     @torch.no_grad()

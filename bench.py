@@ -140,13 +140,14 @@ def kernel_work(rs: dict, T: int) -> dict:
 class Step:
     """One moe_forward of a fixed workload with resident packed weights and buffers."""
 
-    def __init__(self, pkg, inp, device):
+    def __init__(self, pkg, inp, device, packed=None):
         self.pkg, self.inp, self.dev = pkg, inp, device
         self.lib = pkg._native.cuda_lib()
         self.T = inp["hidden_states"].shape[0]
         self.E = inp["gemm1_weights"].shape[0]
-        self.w13p = pkg.pack_w13(inp["gemm1_weights"])
-        self.w2p = pkg.pack_w2(inp["gemm2_weights"])
+        if packed is None:
+            packed = (pkg.pack_w13(inp["gemm1_weights"]), pkg.pack_w2(inp["gemm2_weights"]))
+        self.w13p, self.w2p = packed
         self.hs = inp["hidden_states_scale"].float().contiguous()
         self.s13 = inp["gemm1_weights_scale"].float().contiguous()
         self.s2 = inp["gemm2_weights_scale"].float().contiguous()
@@ -279,6 +280,124 @@ def cpu_oracle_time(pkg, inp, max_seconds: float, experts=None) -> tuple[float, 
     return dt * scale, desc, len(active)
 
 
+def ref_cuda_leg(cases: dict) -> dict:
+    """The reference's own CUDA extension (kernels/moe.cu, built unchanged for sm_100 by
+    oracle/build_ref.py into oracle/_ref) timed on the same GPU and the same device inputs as this
+    package: the GPU baseline. ``cases`` maps a name to (inputs, our us/layer, our bf16 output)."""
+    from oracle import build_ref
+    if not os.path.exists(build_ref.so_path()):
+        return {"unavailable": "oracle/_ref/moe_fused_ref.so not built (python -m oracle.build_ref)"}
+    from oracle import ref_cuda
+    from oracle import moe_oracle as O
+    mod = build_ref.load()
+    res = {"what": "reference kernels/moe.cu (mma.sync e4m3, fp32 atomicAdd combine) built for sm_100 "
+                   "with its own flags, run_custom's call sequence, CUDA events, same device inputs"}
+    for name, (inp, ours_us, ours_out) in cases.items():
+        rc = ref_cuda.RefCuda(inp, mod)
+        us = rc.time_us(steps=10, warmup=3)
+        ref_out = rc()
+        torch.cuda.synchronize()
+        a = ours_out.view(torch.int16).cpu().numpy().view(np.uint16)
+        b = ref_out.view(torch.int16).cpu().numpy().view(np.uint16)
+        diff = O.check_tolerance(a, b)
+        res[name] = {"ref_us_per_layer": round(us, 2), "ours_us_per_layer": round(ours_us, 2),
+                     "speedup": round(us / ours_us, 2),
+                     "ref_vs_ours": {"max_abs_diff": round(diff["max_abs_err"], 5),
+                                     "elements_outside_ref_tolerance": diff["bad"]}}
+        del rc, ref_out
+        torch.cuda.empty_cache()
+    return res
+
+
+# Configuration 2 of the benchmark description: the workload the N = 1 line is quoted on.
+CFG2 = dict(T=4096, E_local=32, local_expert_offset=0, seed=0, routed_scaling_factor=2.5)
+LAYER_FLOPS_PER_ROUTE = FLOPS_G1_PER_ROUTE + FLOPS_G2_PER_ROUTE   # 88,080,384 (reference bench)
+
+
+def config_1gpu() -> dict:
+    """The `config` object of the N = 1 line (both arms print exactly this)."""
+    return {"workload": "config2_prefill_t4096", "T": CFG2["T"], "E_local": CFG2["E_local"],
+            "experts_total": 256, "local_expert_offset": CFG2["local_expert_offset"],
+            "routed_scaling_factor": CFG2["routed_scaling_factor"], "seed": CFG2["seed"],
+            "parallelism": "1 GPU", "l2": "inputs larger than L2 (1.41 GB FP8 expert weights per step)"}
+
+
+def config_ep(world: int) -> dict:
+    """The `config` object of an N > 1 line (both arms print exactly this)."""
+    return {"workload": "ep_weak_config2_t4096", "T_global": CFG2["T"], "experts_per_rank": 32,
+            "experts_instantiated": 32 * world, "experts_total": 256,
+            "routed_scaling_factor": CFG2["routed_scaling_factor"], "seed": CFG2["seed"],
+            "parallelism": f"ep{world}: dispatch/combine as peer stores over NVLink",
+            "placement": "experts 0..32N-1 balanced over the ranks by the route counts of a calibration "
+                         "batch (seed-1 tokens routed with this layer's bias)",
+            "token_count": "each token counted once per 32-expert slice it passes through "
+                           f"({CFG2['T']} x {world} per step); N=8 is the full 256-expert layer",
+            "l2": "inputs larger than L2 (1.41 GB FP8 expert weights per rank per step)"}
+
+
+def layer_work(rs: dict, T: int) -> dict:
+    """Algorithmic HBM bytes and FLOPs of one layer call: every active expert's FP8 weights and
+    scales once, the token rows, scales and logits in, the bf16 output out; FLOPs = local routes
+    x 88,080,384 (the reference benchmark's count, bench/bench_moe.py:32)."""
+    per_expert = W13_EXPERT_BYTES + W2_EXPERT_BYTES + W13_SCALE_BYTES + W2_SCALE_BYTES
+    return dict(bytes=rs["active"] * per_expert + T * (7168 + 224 + 1024) + 512 + T * 14336,
+                flops=rs["routes"] * LAYER_FLOPS_PER_ROUTE)
+
+
+SWEEP_T = [1, 4, 32, 64, 256, 2048, 4096, 8192, 16384]   # reference bench/bench_moe.py:20
+
+
+def t_sweep(pkg, base_inp, packed, device, peaks) -> list:
+    """One GPU, experts 0-31 of configuration 2's weights, T over the reference benchmark's list.
+    Tokens from seed 0, except T = 1, whose seed-0 token routes to no local expert: the probe uses
+    seed 1 (two local routes) so the latency includes the expert GEMMs."""
+    fp8 = 2.0 * peaks["bf16_tflops"]
+    out = []
+    for T in SWEEP_T:
+        seed = 1 if T == 1 else 0
+        act = pkg.make_inputs(pkg.CONFIGS[2].with_(T=T, seed=seed, E_local=1), device)
+        inp = dict(act, **{k: base_inp[k] for k in ("gemm1_weights", "gemm1_weights_scale",
+                                                    "gemm2_weights", "gemm2_weights_scale")})
+        step = Step(pkg, inp, device, packed=packed)
+        rs = routing_stats(pkg, inp)
+        for _ in range(3):
+            step()
+        n = 20 if T <= 4096 else 10
+        us = time_steps(step, n) / n * 1e3
+        w = layer_work(rs, T)
+        out.append({"T": T, "seed": seed, "us_per_layer": round(us, 2),
+                    "tokens_per_s": round(T / (us * 1e-6), 1), "routes": rs["routes"],
+                    "active_experts": rs["active"], "bytes": int(w["bytes"]), "flops": int(w["flops"]),
+                    "hbm_frac": round(w["bytes"] / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4),
+                    "fp8_tc_frac": round(w["flops"] / (us * 1e-6) / 1e12 / fp8, 4)})
+        del step, inp, act
+    torch.cuda.empty_cache()
+    return out
+
+
+def slice_spread(pkg, device, peaks, steps: int = 10) -> list:
+    """Configuration 2's tokens (T = 4096, seed 0) on each 32-expert slice of the 256-expert layer
+    (local_expert_offset 0, 32, ..., 224): the headline instance is slice 0."""
+    act = pkg.make_inputs(pkg.CONFIGS[2].with_(E_local=1), device)
+    out = []
+    for off in range(0, 256, 32):
+        cfg = pkg.CONFIGS[2].with_(local_expert_offset=off)
+        inp = dict(act, **pkg.make_weights(cfg, range(off, off + 32), device), local_expert_offset=off)
+        step = Step(pkg, inp, device)
+        rs = routing_stats(pkg, inp)
+        for _ in range(3):
+            step()
+        us = time_steps(step, steps) / steps * 1e3
+        w = layer_work(rs, cfg.T)
+        out.append({"local_expert_offset": off, "routes": rs["routes"], "active_experts": rs["active"],
+                    "max_routes_per_expert": rs["max_per_expert"], "us_per_layer": round(us, 2),
+                    "tokens_per_s": round(cfg.T / (us * 1e-6), 1),
+                    "hbm_frac": round(w["bytes"] / (us * 1e-6) / 1e9 / peaks["hbm_gbs"], 4)})
+        del step, inp
+        torch.cuda.empty_cache()
+    return out
+
+
 def make_workload(pkg, name: str, rank: int, device):
     base = pkg.CONFIGS[2] if name == "prefill" else pkg.CONFIGS[1]
     cfg = base.with_(local_expert_offset=32 * (rank % 8))
@@ -358,6 +477,10 @@ def bench_ours(args, rank, world, local_rank, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         e2e["ms_per_step"] = float(t.item())
 
+    # The reference benchmark's T list on one GPU, and configuration 2's tokens on every slice.
+    sweep = t_sweep(pkg, inp, (step.w13p, step.w2p), device, peaks)
+    spread = slice_spread(pkg, device, peaks)
+
     if rank != 0:
         return None
     tokens = cfg.T * world
@@ -375,20 +498,23 @@ def bench_ours(args, rank, world, local_rank, dist):
         "dtype": "e4m3 (fp32 accumulate)",
         "data": "synthetic: seeded N(0,1) logits/hidden, N(0,0.1) bias, N(0,0.02) weights, "
                 "e4m3 with amax/448 128-block scales",
-        "config": {"workload": "config2_prefill_t4096", "T": cfg.T, "E_local": cfg.E_local,
-                   "experts_total": 256, "local_expert_offset": "32*rank",
-                   "routed_scaling_factor": cfg.routed_scaling_factor, "seed": cfg.seed,
-                   "routes": rs["routes"], "active_experts": rs["active"],
-                   "max_routes_per_expert": rs["max_per_expert"], "tiles": rs["tiles"],
-                   "parallelism": f"{world} x independent 32-expert slices" if world > 1 else "1 GPU",
-                   "l2": "inputs larger than L2 (1.41 GB FP8 expert weights per step)"},
+        "config": config_1gpu(),
+        "routing": {"routes": rs["routes"], "active_experts": rs["active"],
+                    "max_routes_per_expert": rs["max_per_expert"], "tiles": rs["tiles"]},
         "roofline": roof,
+        "layer_roofline": (lambda w: {"bytes": int(w["bytes"]), "flops": int(w["flops"]),
+                                      "hbm_frac": round(w["bytes"] / (ms / args.steps * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+                                      "fp8_tc_frac": round(w["flops"] / (ms / args.steps * 1e-3) / 1e12 / (2.0 * peaks["bf16_tflops"]), 4),
+                                      "fp8_peak": "derived: 2 x measured bf16 burst"})(layer_work(rs, cfg.T)),
         "stage_us": {k: round(v * 1e3, 2) for k, v in stages.items()},
         "decode_t64": {"us_per_layer": round(dms * 1e3, 2), "routes": drs["routes"],
                        "active_experts": drs["active"],
                        "weight_bytes": int(layer_bytes),
                        "hbm_frac_layer": round(layer_bytes / (dms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                        "roofline": droof, "stage_us": {k: round(v * 1e3, 2) for k, v in dstages.items()}},
+        "t_sweep": sweep,
+        "t1_probe": next(x for x in sweep if x["T"] == 1),
+        "slices_t4096": spread,
         "quantize": {"T": TQ, "us": round(q_ms * 1e3, 2), "bytes": q_bytes,
                      "achieved_gbs": round(q_bytes / (q_ms * 1e-3) / 1e9, 1),
                      "hbm_frac": round(q_bytes / (q_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
@@ -407,6 +533,14 @@ def bench_ours(args, rank, world, local_rank, dist):
         "clocks": clocks,
         "device_status": status,
     }
+    if world == 1:
+        out_p, out_d = torch.empty_like(step.out), torch.empty_like(dstep.out)
+        step()
+        out_p.copy_(step.out)
+        dstep()
+        out_d.copy_(dstep.out)
+        line["ref_cuda"] = ref_cuda_leg({"config2_t4096": (inp, ms * 1e3 / args.steps, out_p),
+                                         "config1_t64": (dinp, dms * 1e3, out_d)})
     if world == 1 and not args.no_cpu_baseline:
         secs, desc, _ = cpu_oracle_time(pkg, {k: (v.cpu() if isinstance(v, torch.Tensor) else v)
                                               for k, v in inp.items()}, 30.0)
@@ -509,7 +643,8 @@ def bench_ep(args, rank, world, local_rank, dist):
         stages = {n: statistics.mean(evs[r][i].elapsed_time(evs[r][i + 1]) for r in range(reps))
                   for i, n in enumerate(names)}
         work = kernel_work(rs, T_r)
-        roof = roofline(stages, work, peaks, load_traffic("prefill_t4096") if rank == 0 else None)
+        # No ncu capture of these per-rank workloads exists, so no traffic figure is reported.
+        roof = roofline(stages, work, peaks, None)
 
         # Every rank's load and stage times (the slowest rank sets the step).
         names_all = list(stages)
@@ -548,17 +683,9 @@ def bench_ep(args, rank, world, local_rank, dist):
         "dtype": "e4m3 (fp32 accumulate)",
         "data": "synthetic: seeded N(0,1) logits/hidden, N(0,0.1) bias, N(0,0.02) weights, "
                 "e4m3 with amax/448 128-block scales",
-        "config": {"workload": "ep_weak_config2_t4096", "T_global": T_global, "T_per_rank": T_r,
-                   "experts_per_rank": e_rank, "experts_instantiated": e_rank * world,
-                   "experts_total": 256, "routed_scaling_factor": cfg.routed_scaling_factor,
-                   "seed": cfg.seed, "parallelism": f"ep{world}: dispatch/combine as peer stores over NVLink",
-                   "placement": "experts 0..32N-1 balanced over the ranks by the route counts of a calibration "
-                                "batch (seed-1 tokens routed with this layer's bias)",
-                   "token_count": "each token counted once per 32-expert slice it passes through "
-                                  f"({T_global} x {world} per step); N=8 is the full 256-expert layer",
-                   "routes_all_ranks": int(routes_all.item()), "routes_rank0": rs["routes"],
-                   "active_experts_rank0": rs["active"],
-                   "l2": "inputs larger than L2 (1.41 GB FP8 expert weights per rank per step)"},
+        "config": config_ep(world),
+        "routing": {"T_per_rank": T_r, "routes_all_ranks": int(routes_all.item()), "routes_rank0": rs["routes"],
+                    "active_experts_rank0": rs["active"]},
         "layer_tokens_per_s": round(T_global * args.steps / (ms * 1e-3), 1),
         "roofline": roof,
         "stage_us_rank0": {kk: round(v * 1e3, 2) for kk, v in stages.items()},
@@ -577,44 +704,73 @@ def bench_ep(args, rank, world, local_rank, dist):
     }
 
 
-def bench_reference(args, rank):
-    """CPU restatement of the reference (oracle/) on the host cores, same config / metric."""
+def bench_reference(args, rank, world):
+    """The reference's algorithm on the host CPU cores (oracle/moe_oracle.py, the numpy
+    restatement of reference/moe_ref.py; the reference itself is Python and cannot travel), on
+    the same configuration, metric and unit as this package's arm at the same N. Inputs come from
+    oracle/synth_oracle.py (numpy restatement of the package's generator, same bytes), so this
+    arm loads none of the package's compiled code.
+
+    Unit of work: one 32-expert slice of the layer over configuration 2's 4096 tokens (a
+    moe_ref.run call; local_expert_offset = 32 r), all of its active experts. At N = 1 that is
+    the whole workload and every step times it. At N > 1 the workload is N slices and the unit
+    (token-slices) adds over slices, so step i times slice i mod N and the value is
+    4096 N / (sum over slices of their mean step time). Rank 0 alone runs; the others exit."""
     if rank != 0:
         return None
-    pkg = importlib.import_module("15642_moe_b200")
-    cfg = pkg.CONFIGS[2]
-    inp = pkg.make_inputs(cfg, "cuda:0" if torch.cuda.is_available() else "cpu")
-    inp = {k: (v.cpu() if isinstance(v, torch.Tensor) else v) for k, v in inp.items()}
     from oracle import moe_oracle as O
-    npi = O.to_numpy_inputs(inp)
-    idx, _ = O.route(npi["routing_logits"], npi["routing_bias"], npi["routed_scaling_factor"])
-    active = [e for e in range(32) if (idx == e).any()]
-    # First warm-up call on the full layer sizes the per-step sample so the run stays bounded.
-    t0 = time.perf_counter()
-    O.moe_forward(**npi, experts=active[:2])
-    per_expert = (time.perf_counter() - t0) / 2
-    budget = 150.0 / max(1, args.steps + args.warmup)
-    n_s = int(max(1, min(len(active), budget // max(per_expert, 1e-3))))
-    times = []
+    from oracle import synth_oracle as S
+    T, seed, rsf = CFG2["T"], CFG2["seed"], CFG2["routed_scaling_factor"]
+    logits = S.logits(seed, T)
+    bias = (S.bias_bits(seed, 0.1, (), 1.5).astype(np.uint32) << 16).view(np.float32)
+    hid, hsc = S.hidden(seed, T)
+    idx, _ = O.route(logits, bias, rsf)
+    slices, stats = [], []
+    for r in range(world):
+        off = 32 * r
+        sel = idx[(idx >= off) & (idx < off + 32)] - off
+        counts = np.bincount(sel.ravel(), minlength=32)
+        active = [e for e in range(32) if counts[e] > 0]
+        w13 = np.zeros((32, 4096, 7168), np.uint8)
+        s13 = np.zeros((32, 32, 56), np.float32)
+        w2 = np.zeros((32, 7168, 2048), np.uint8)
+        s2 = np.zeros((32, 56, 16), np.float32)
+        if active:
+            a, b, c, d = S.weights(seed, [off + e for e in active])
+            w13[active], s13[active], w2[active], s2[active] = a, b, c, d
+        npi = dict(routing_logits=logits, routing_bias=bias, hidden_states=hid, hidden_states_scale=hsc,
+                   gemm1_weights=w13, gemm1_weights_scale=s13, gemm2_weights=w2, gemm2_weights_scale=s2,
+                   local_expert_offset=off, routed_scaling_factor=rsf)
+        O.moe_forward(**npi, experts=active)      # first call pays the page faults; discarded
+        slices.append((npi, active))
+        stats.append({"local_expert_offset": off, "routes": int(counts.sum()), "active_experts": len(active)})
+    times = [[] for _ in range(world)]
     for i in range(args.warmup + args.steps):
-        sample = [active[(i * n_s + j) % len(active)] for j in range(n_s)]
+        r = i % world
+        npi, active = slices[r]
         t0 = time.perf_counter()
-        O.moe_forward(**npi, experts=sample)
-        dt = (time.perf_counter() - t0) * len(active) / n_s
+        O.moe_forward(**npi, experts=active)
+        dt = time.perf_counter() - t0
         if i >= args.warmup:
-            times.append(dt)
-    secs = statistics.mean(times)
-    value = cfg.T / secs
-    sample_desc = (f"per step {n_s} of {len(active)} active local experts (rotating), full routing, "
-                   f"time scaled x{len(active) / n_s:.2f}; oracle/moe_oracle.py numpy restatement of "
-                   f"reference/moe_ref.py")
+            times[r].append(dt)
+    timed = [statistics.mean(t) for t in times if t]
+    secs = statistics.mean(timed) * world      # CPU seconds of the whole workload of one step
+    value = T * world / secs
+    cores = os.cpu_count()
+    sample = (f"oracle/moe_oracle.py (numpy restatement of reference/moe_ref.py), T={T}, "
+              + ("the full layer (all active local experts) every step" if world == 1 else
+                 f"step i = 32-expert slice i mod {world} with all its active experts; "
+                 f"{sum(1 for t in times if t)} of {world} slices timed")
+              + f"; numpy/BLAS on {cores} host threads")
     return {"metric": METRIC, "value": round(value, 2), "unit": "tokens/s", "impl": "reference",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
             "ms_per_step": round(secs * 1e3, 2), "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f32", "data": "synthetic (same generator and seed)",
-            "config": {"workload": "config2_prefill_t4096", "T": cfg.T, "E_local": 32},
-            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": os.cpu_count(),
-                             "kind": "port", "sample": sample_desc},
+            "vs_baseline": None, "dtype": "f32",
+            "data": "synthetic (same generator and seed, restated in numpy: oracle/synth_oracle.py)",
+            "config": config_1gpu() if world == 1 else config_ep(world),
+            "routing_slices": stats,
+            "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": cores,
+                             "kind": "port", "sample": sample},
             "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
 
@@ -639,7 +795,7 @@ def main():
     local_rank = int(os.environ.get("LOCAL_RANK", "0"))
 
     if args.impl == "reference":
-        line = bench_reference(args, rank)
+        line = bench_reference(args, rank, world)
         if line is not None:
             print(json.dumps(line), file=result_out, flush=True)
         return

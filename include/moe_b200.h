@@ -46,6 +46,24 @@ const char* moe_last_error(void);
  * reference never checks kernel-side failures. */
 int moe_get_status(int* status, int reset);
 
+/* Limit of every bounded wait in the kernels (mbarrier waits of the GEMM roles, the
+ * expert-parallel flag barriers) on the current device, in nanoseconds; 2 s by default,
+ * accepted range [1 ms, 60 s]. A wait that runs out sets its status bit and returns. No
+ * reference counterpart (the reference has no waits). Synchronous. */
+int moe_set_wait_limit_ns(unsigned long long ns);
+int moe_get_wait_limit_ns(unsigned long long* ns);
+
+/* Failure-path probes: each makes one bounded wait run out on purpose, on the host's request,
+ * without a fault, so tests can check that the kernel returns and reports it.
+ * moe_probe_ep_barrier_timeout: the expert-parallel barrier kernel of a 2-rank layout whose
+ *   second rank never signals; buf = >= 256 zeroed device bytes standing for both ranks'
+ *   buffers. Sets status bit 16 after the wait limit.
+ * moe_probe_mbar_timeout: one thread waits on an mbarrier nothing arrives on; after the wait
+ *   limit it sets status bit `who` (1, 2 or 4) and writes *aborted (device int) = 1.
+ * No reference counterpart. */
+int moe_probe_ep_barrier_timeout(void* buf, void* stream);
+int moe_probe_mbar_timeout(int who, int* aborted, void* stream);
+
 /* Bytes of the packed W13 for E_local experts (the reference returns an int32 tensor of
  * the same byte count, kernels/moe.cu:712). */
 size_t moe_pack_w13_bytes(int E_local);

@@ -13,6 +13,12 @@ GPU generator); the script stores
                                        detect any drift of the generator,
   * the configuration fields.
 Routing-only cases stop the reference right after its top-8 selection.
+
+``ref_t*`` cases use the reference's OWN test generator instead (``moe_layer.build_moe_inputs``
+on the CPU, ``seed = T`` as ``tests/test_moe.py:44`` calls it: uniform e4m3 values, U(0.01,
+0.11) scales, zero bias, routed_scaling_factor 1) at the reference test's token counts up to
+256 (``tests/test_moe.py:18``). They store the same fields; ``tests/ref_inputs.py`` restates
+that generator and must reproduce the stored digests.
 """
 from __future__ import annotations
 
@@ -41,6 +47,11 @@ CASES = [
     ("route_cfg2_t4096", 2, {}, True),
     ("route_cfg4_t16384_skew", 4, {"E_local": 32}, True),
 ]
+
+
+# The reference test's token counts that fit a committed fixture (T = 2048 and up: the
+# oracle-parity tests on the GPU cover those sizes).
+REF_CASES = [1, 4, 32, 64, 256]
 
 
 class _Stop(Exception):
@@ -98,6 +109,24 @@ def main():
             rec["out_bf16"] = out.contiguous().view(torch.int16).numpy().view(np.uint16)
         np.savez_compressed(os.path.join(HERE, f"{name}.npz"), **rec)
         print(name, "T=%d" % cfg.T, "routing_only" if routing_only else "full", flush=True)
+    moe_layer = importlib.import_module("moe_layer")
+    sys.path.insert(0, os.path.dirname(HERE))
+    ref_inputs = importlib.import_module("ref_inputs")
+    for T in REF_CASES:
+        name = f"ref_t{T}"
+        if args.only and name != args.only:
+            continue
+        inputs = moe_layer.build_moe_inputs(T, device="cpu", seed=T)
+        dig = digests(inputs)
+        mine = ref_inputs.digests(ref_inputs.build_moe_inputs(T, T))
+        assert mine == dig, f"tests/ref_inputs.py does not reproduce the reference generator at T={T}"
+        out, idx = run_reference(reference, inputs, False)
+        cfg = dict(generator="reference moe_layer.build_moe_inputs (cpu)", T=T, seed=T,
+                   local_expert_offset=0, routed_scaling_factor=1.0)
+        np.savez_compressed(os.path.join(HERE, f"{name}.npz"), topk_sorted=idx, config=json.dumps(cfg),
+                            inputs_sha256=json.dumps(dig),
+                            out_bf16=out.contiguous().view(torch.int16).numpy().view(np.uint16))
+        print(name, "T=%d" % T, "full (reference generator)", flush=True)
 
 
 if __name__ == "__main__":

@@ -8,9 +8,20 @@ import sys
 REPO = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 
 
+# Runs bench.py's reference arm as __main__, then reports on standard error whether any of the
+# package's compiled libraries was mapped into the process (the arm must load none of them).
+_WRAPPER = """
+import runpy, sys
+sys.argv = [sys.argv[1], "--impl", "reference", "--steps", "1", "--warmup", "3"]
+runpy.run_path(sys.argv[0], run_name="__main__")
+maps = open("/proc/self/maps").read()
+sys.stderr.write("PACKAGE_SO_MAPPED=%d\\n" % ("15642_moe_b200/lib" in maps))
+"""
+
+
 def test_reference_arm_prints_one_json_line():
-    res = subprocess.run([sys.executable, os.path.join(REPO, "bench.py"), "--impl", "reference", "--steps", "1",
-                          "--warmup", "3"], capture_output=True, text=True, timeout=600, cwd=REPO)
+    res = subprocess.run([sys.executable, "-c", _WRAPPER, os.path.join(REPO, "bench.py")],
+                         capture_output=True, text=True, timeout=900, cwd=REPO)
     assert res.returncode == 0, res.stderr[-2000:]
     lines = res.stdout.splitlines()
     assert len(lines) == 1, res.stdout[-2000:]
@@ -22,3 +33,8 @@ def test_reference_arm_prints_one_json_line():
     assert d["cpu_baseline"]["kind"] in ("port", "reference") and d["cpu_baseline"]["cores"] >= 1
     assert d["cpu_baseline"]["value"] == d["value"]
     assert d["e2e"]["h2d_bytes_per_step"] == 0 and d["e2e"]["d2h_bytes_per_step"] == 0
+    # same configuration object as this package's arm at N = 1, no compiled package code loaded
+    sys.path.insert(0, REPO)
+    import bench
+    assert d["config"] == bench.config_1gpu()
+    assert "PACKAGE_SO_MAPPED=0" in res.stderr, res.stderr[-2000:]

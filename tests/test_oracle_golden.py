@@ -86,3 +86,24 @@ def test_planted_mistake_is_caught(cpu_inputs, oracle, monkeypatch):
 
     out = swapped(**oracle.to_numpy_inputs(cpu_inputs("cfg0_t16")))
     assert oracle.check_tolerance(g["out_bf16"], out)["bad"] > 1000
+
+
+# Goldens on the reference test suite's own inputs (moe_layer.build_moe_inputs, seed = T;
+# restated in tests/ref_inputs.py). T = 256 takes a few seconds more than the others.
+REF_FULL = ["ref_t1", "ref_t4", "ref_t32", "ref_t64", "ref_t256"]
+
+
+@pytest.mark.parametrize("name", REF_FULL)
+def test_oracle_matches_reference_on_its_own_generator(name, oracle):
+    from ref_inputs import build_moe_inputs, digests as ref_digests
+    g, cfg = load(name)
+    inp = build_moe_inputs(cfg["T"], cfg["seed"])
+    assert ref_digests(inp) == json.loads(str(g["inputs_sha256"])), "generator restatement drifted"
+    out, idx, _ = oracle.moe_forward(**oracle.to_numpy_inputs(inp), return_routing=True)
+    np.testing.assert_array_equal(np.sort(idx, axis=1), g["topk_sorted"])
+    r = oracle.check_tolerance(g["out_bf16"], out)
+    assert r["bad"] == 0, r
+    diff = np.abs(oracle.bf16_bits_to_f32(out) - oracle.bf16_bits_to_f32(g["out_bf16"]))
+    ulp = np.abs(oracle.bf16_bits_to_f32(g["out_bf16"])) * 2.0 ** -7 + 2.0 ** -20
+    assert (diff <= ulp).all(), float(diff.max())
+    assert (out == g["out_bf16"]).mean() > 0.99

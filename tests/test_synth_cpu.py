@@ -56,3 +56,25 @@ def test_skew_bias(pkg):
     b = pkg.make_inputs(cfg, "cpu")["routing_bias"].float()
     hot = list(cfg.hot_experts)
     assert len(hot) == 16 and (b[hot] == 1.5).all()
+
+
+def test_oracle_generator_restatement_matches(pkg, oracle):
+    """oracle/synth_oracle.py (numpy, used by the benchmark's CPU arms so they load no compiled
+    code of the package) produces the package generator's bytes: a slice with hot experts, an
+    offset and a seed other than 0, and the e4m3 encoder against torch's cast on edge values."""
+    from oracle import synth_oracle as S
+    cfg = pkg.MoEConfig(T=48, E_local=2, local_expert_offset=31, seed=9, hot_experts=(0, 1, 32))
+    a = oracle.to_numpy_inputs(pkg.make_inputs(cfg, "cpu"))
+    b = S.make_inputs(**cfg.__dict__)
+    for k, v in a.items():
+        if isinstance(v, np.ndarray):
+            assert np.array_equal(v.view(np.uint8), np.ascontiguousarray(b[k]).view(np.uint8)), k
+        else:
+            assert v == b[k], k
+    part = S.make_inputs(**cfg.__dict__, experts=[1])
+    assert np.array_equal(part["gemm2_weights"][1], b["gemm2_weights"][1]) and not part["gemm1_weights"][0].any()
+    x = np.concatenate([np.random.default_rng(0).standard_normal(1 << 16).astype(np.float32) * 50,
+                        np.array([0, -0.0, 448, 463.9, 2 ** -9, 2 ** -10, 3 * 2 ** -11, -2 ** -7, 1e-30],
+                                 np.float32)])
+    ref = torch.from_numpy(x).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(S.e4m3_codes(x), ref)

@@ -57,6 +57,10 @@ def test_noalloc_matches_moe_forward_twice(pkg, oracle):
         torch.cuda.synchronize()
         a = ref.view(torch.int16).cpu().numpy().view(np.uint16)
         b = out.view(torch.int16).cpu().numpy().view(np.uint16)
+        # Both entry points run the same deterministic kernels on the same inputs, so the
+        # outputs must agree bit for bit; a stale-scratch bug smaller than the tolerance
+        # would still show here.
+        np.testing.assert_array_equal(a, b, err_msg=str(cfg))
         r = oracle.check_tolerance(a, b, ATOL, RTOL)
         assert r["bad"] == 0, (cfg, r)
         assert np.isfinite(oracle.bf16_bits_to_f32(b)).all()
