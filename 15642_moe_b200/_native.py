@@ -152,7 +152,7 @@ def wait_limit_ns() -> int:
 def workspace_layout(T: int, E_local: int) -> dict:
     names = ["counts", "dense_base", "topk_idx", "topk_w", "token_nr", "token_route",
              "route_token", "route_w", "a_tiled", "a_scale", "c_hi", "c_lo", "c_scale", "partial",
-             "total"]
+             "tile_ready", "total"]
     arr = (ctypes.c_size_t * len(names))()
     n = cuda_lib().moe_workspace_layout(T, E_local, arr, len(names))
     if n <= 0:

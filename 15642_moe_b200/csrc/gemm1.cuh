@@ -38,6 +38,7 @@ struct Gemm1Args {
   uint8_t* c_hi;            // [tiles, 16, 128, 128] SW128
   uint8_t* c_lo;            // [tiles, 16, 128, 128] SW128
   float* c_scale;           // [tiles, 16, 128]
+  int* tile_ready;          // [tiles] column blocks of the tile whose C is stored (release-add)
 };
 
 constexpr int G1_STAGES = 4;
@@ -166,6 +167,9 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (warp == 0) build_tile_map(&ctl->map, p.counts, p.E_local, p.slots, p.tiles_max);
   __syncthreads();
+  // GEMM2 may be scheduled on SMs as soon as every CTA of this grid is resident; it waits per
+  // tile on tile_ready, so it never needs this grid to finish.
+  if (threadIdx.x == 0) allow_dependent_launch();
   const int n_units = clamp_tiles(ctl->map.tile_off[p.E_local], p.tiles_max) * G1_NT;
   if (static_cast<int>(blockIdx.x) >= n_units) return;  // uniform per CTA, before any TMEM use
 
@@ -346,6 +350,11 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
         *reinterpret_cast<uint4*>(p.c_lo + off) = lo;
       }
       if (hf == 0) p.c_scale[(static_cast<size_t>(tile) * IB + j) * TILE_M + row] = scale;
+      // Publish: once every epilogue thread's C stores of this unit are visible GPU-wide, count
+      // the column block as done for the tile (GEMM2 starts a tile at G1_NT).
+      __threadfence();
+      named_bar_or(3, 256, false);
+      if (warp == 4 && lane == 0) red_release_add(p.tile_ready + tile, 1);
     }
   }
 

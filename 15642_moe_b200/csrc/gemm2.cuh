@@ -35,7 +35,27 @@ struct Gemm2Args {
   const float* route_w;     // [E_local, slots] routing weight of each expert slot
   float* partial;           // [routes, 7168] dense: route (e, slot) is row dense_base[e] + slot
   int* dense_base;          // [E_local + 1] written by CTA 0 for the combine
+  const int* tile_ready;    // [tiles] GEMM1 column blocks done per tile; a tile is read at G1_NT
 };
+
+// Bounded wait until GEMM1 has stored all G1_NT column blocks of C for `tile` (acquire), then
+// order the following bulk copies (async proxy) after it. Returns false on timeout or abort.
+__device__ __forceinline__ bool wait_tile_ready(const int* ready, volatile int* abort_flag) {
+  if (ld_acquire_gpu(ready) < G1_NT) {
+    const unsigned long long t0 = globaltimer(), limit = wait_limit_ns();
+    while (ld_acquire_gpu(ready) < G1_NT) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > limit) {
+        *abort_flag = 1;
+        report_status(ST_TIMEOUT_PRODUCER);
+        return false;
+      }
+      __nanosleep(256);
+    }
+  }
+  fence_proxy_async_global();
+  return true;
+}
 
 constexpr int G2_STAGES = 3;
 constexpr int G2_A_BYTES = TILE_BYTES;      // one of hi / lo
@@ -102,11 +122,18 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
       uint32_t it = 0;
+      int ready_tile = -1;
       for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
         const int tile = u / G2_NT, nt = u % G2_NT;
         const int e = tile_expert(&ctl->map, p.E_local, tile);
         const size_t a_off = static_cast<size_t>(tile) * IB * TILE_BYTES;
         const uint8_t* b_src = p.w2p + (static_cast<size_t>(e) * G2_NT + nt) * IB * G2_B_BYTES;
+        // This grid may start while GEMM1 still runs (programmatic launch): the tile's C must be
+        // complete before its first copy is issued.
+        if (tile != ready_tile) {
+          if (!wait_tile_ready(p.tile_ready + tile, abort_flag)) break;
+          ready_tile = tile;
+        }
         for (int ib = 0; ib < IB; ++ib, ++it) {
           const int s = it % G2_STAGES;
           const uint32_t ph = (it / G2_STAGES) & 1u;
@@ -197,12 +224,14 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
-      float nc = __ldg(cs_ptr), n0 = __ldg(ws0), n1 = __ldg(ws1);
-      bool aborted = false;
-      for (int ib = 0; ib < IB; ++ib, ++it) {
+      // c_scale is written by GEMM1, which may still be running: acquire the tile's counter
+      // first (it is complete by now unless this CTA is far ahead), then read through L2.
+      bool aborted = !wait_tile_ready(p.tile_ready + tile, abort_flag);
+      float nc = aborted ? 0.0f : __ldcg(cs_ptr), n0 = __ldg(ws0), n1 = __ldg(ws1);
+      for (int ib = 0; ib < IB && !aborted; ++ib, ++it) {
         const float f0 = nc * n0, f1 = nc * n1;
         if (ib + 1 < IB) {
-          nc = __ldg(cs_ptr + (ib + 1) * TILE_M);
+          nc = __ldcg(cs_ptr + (ib + 1) * TILE_M);
           n0 = __ldg(ws0 + ib + 1);
           n1 = __ldg(ws1 + ib + 1);
         }

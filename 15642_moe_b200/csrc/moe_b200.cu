@@ -145,6 +145,23 @@ int hidden_bf16_map(const void* hidden, int T, CUtensorMap* map) {
   return MOE_OK;
 }
 
+// GEMM2 launched so that it may start on SMs that GEMM1's CTAs have left while GEMM1 still runs
+// (programmatic dependent launch; GEMM1 allows it once all its CTAs are resident, GEMM2 waits per
+// tile on the readiness counters GEMM1 publishes).
+cudaError_t launch_gemm2(const Gemm2Args& g2, int grid, cudaStream_t st) {
+  cudaLaunchConfig_t cfg{};
+  cfg.gridDim = dim3(static_cast<unsigned>(grid));
+  cfg.blockDim = dim3(G2_THREADS);
+  cfg.dynamicSmemBytes = G2_SMEM;
+  cfg.stream = st;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, gemm2_weighted_kernel, g2);
+}
+
 int grid_for(size_t work, int per_block, int cap) {
   size_t g = (work + per_block - 1) / per_block;
   if (g < 1) g = 1;
@@ -236,11 +253,11 @@ size_t moe_forward_workspace_bytes(int T, int E_local) {
 int moe_workspace_layout(int T, int E_local, size_t* offsets, int n) {
   if (T < 0 || E_local < 1 || E_local > E_GLOBAL) return fail(MOE_ERR_INVALID, "bad T or E_local");
   const Workspace w = make_workspace(T, E_local);
-  const size_t v[15] = {w.counts,  w.dense_base, w.topk_idx, w.topk_w,  w.token_nr,
+  const size_t v[16] = {w.counts,  w.dense_base, w.topk_idx, w.topk_w,  w.token_nr,
                         w.token_route, w.route_token, w.route_w, w.a_tiled, w.a_scale,
-                        w.c_hi,    w.c_lo,       w.c_scale,  w.partial, w.total};
-  for (int i = 0; i < n && i < 15; ++i) offsets[i] = v[i];
-  return 15;
+                        w.c_hi,    w.c_lo,       w.c_scale,  w.partial, w.tile_ready, w.total};
+  for (int i = 0; i < n && i < 16; ++i) offsets[i] = v[i];
+  return 16;
 }
 
 }  // extern "C"
@@ -289,10 +306,11 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
 
   uint8_t* a_tiled = W + ws.a_tiled;
   float* a_scale = reinterpret_cast<float*>(W + ws.a_scale);
+  int* tile_ready = reinterpret_cast<int*>(W + ws.tile_ready);
   Gemm1Args g1{a_tiled, a_scale, static_cast<const uint8_t*>(w13_packed), w13_scale, counts, T,
-               ws.tiles_max, E_local, c_hi, c_lo, c_scale};
+               ws.tiles_max, E_local, c_hi, c_lo, c_scale, tile_ready};
   Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, counts, T,
-               ws.tiles_max, E_local, route_w, partial, dense_base};
+               ws.tiles_max, E_local, route_w, partial, dense_base, tile_ready};
 
   auto mark = [&](int i) {
     if (events != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
@@ -310,13 +328,13 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   const size_t route_max = static_cast<size_t>(T) * (E_local < TOP_K ? E_local : TOP_K);
   gather_kernel<<<grid_for(route_max, 8, d->num_sms * 8), 256, 0, st>>>(
       static_cast<const uint8_t*>(hidden), hidden_scale, T, counts, E_local, route_token,
-      ws.tiles_max, a_tiled, a_scale);
+      ws.tiles_max, a_tiled, a_scale, tile_ready);
   mark(2);
   const int g1_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G1_NT, 1, d->num_sms);
   gemm1_swiglu_kernel<<<g1_grid, G1_THREADS, G1_SMEM, st>>>(g1);
   mark(3);
   const int g2_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G2_NT, 1, d->num_sms);
-  gemm2_weighted_kernel<<<g2_grid, G2_THREADS, G2_SMEM, st>>>(g2);
+  if (int rc = cuda_check(launch_gemm2(g2, g2_grid, st), "gemm2 launch")) return rc;
   mark(4);
   if (out_f32)
     combine_kernel<float><<<T, COMBINE_THREADS, 0, st>>>(partial, token_nr, token_route, dense_base, T,
@@ -387,10 +405,11 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
   uint8_t* c_lo = W + ws.c_lo;
   float* c_scale = reinterpret_cast<float*>(W + ws.c_scale);
   float* partial = reinterpret_cast<float*>(W + ws.partial);
+  int* tile_ready = reinterpret_cast<int*>(W + ws.tile_ready);
   Gemm1Args g1{a_tiled, a_scale, static_cast<const uint8_t*>(w13_packed), w13_scale, counts, L.r_cap,
-               ws.tiles_max, L.e_rank, c_hi, c_lo, c_scale};
+               ws.tiles_max, L.e_rank, c_hi, c_lo, c_scale, tile_ready};
   Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, counts, L.r_cap,
-               ws.tiles_max, L.e_rank, ep_at<float>(me, L.route_w), partial, dense_base};
+               ws.tiles_max, L.e_rank, ep_at<float>(me, L.route_w), partial, dense_base, tile_ready};
   // Source side: local slot claims over all 256 experts (route_kernel with E_local = 256).
   int* local_counts = reinterpret_cast<int*>(W + sw.local_counts);
   int* reserve_base = reinterpret_cast<int*>(W + sw.base);
@@ -420,11 +439,13 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
   const size_t route_max = static_cast<size_t>(L.r_cap) * (L.e_rank < TOP_K ? L.e_rank : TOP_K);
   gather_kernel<<<grid_for(route_max, 8, d->num_sms * 8), 256, 0, st>>>(
       me + L.recv_rows, ep_at<float>(me, L.recv_scale), L.r_cap, counts, L.e_rank,
-      ep_at<int>(me, L.route_token), ws.tiles_max, a_tiled, a_scale);
+      ep_at<int>(me, L.route_token), ws.tiles_max, a_tiled, a_scale, tile_ready);
   mark(4);
   gemm1_swiglu_kernel<<<grid_for(static_cast<size_t>(ws.tiles_max) * G1_NT, 1, d->num_sms), G1_THREADS, G1_SMEM, st>>>(g1);
   mark(5);
-  gemm2_weighted_kernel<<<grid_for(static_cast<size_t>(ws.tiles_max) * G2_NT, 1, d->num_sms), G2_THREADS, G2_SMEM, st>>>(g2);
+  if (int rc = cuda_check(launch_gemm2(g2, grid_for(static_cast<size_t>(ws.tiles_max) * G2_NT, 1, d->num_sms), st),
+                          "gemm2 launch"))
+    return rc;
   mark(6);
   ep_combine_send_kernel<<<grid_for(static_cast<size_t>(L.r_cap), 1, d->num_sms * 4), COMBINE_THREADS, 0, st>>>(
       c->peers, L, c->rank, partial, dense_base);

@@ -80,6 +80,26 @@ __device__ __forceinline__ void st_release_sys(unsigned* p, unsigned v) {
   asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
 
+// GPU-scope release / acquire on a counter in global memory (GEMM1 -> GEMM2 tile hand-off).
+__device__ __forceinline__ void red_release_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+// Order this thread's earlier generic-proxy accesses of global memory before its later
+// async-proxy (bulk copy) accesses.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+// Programmatic dependent launch: allow the next kernel of the stream (launched with the
+// programmatic-serialization attribute) to be scheduled before this grid completes.
+__device__ __forceinline__ void allow_dependent_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // Routing metadata is produced on the device; a consumer never trusts it for addressing.
 __device__ __forceinline__ int clamp_tiles(int n, int tiles_max) {
   if (n < 0 || n > tiles_max) {
@@ -362,6 +382,7 @@ struct Workspace {
   size_t c_lo;         // u8    [tiles_max, 16, 128, 128] e4m3 residual
   size_t c_scale;      // fp32  [tiles_max, 16, 128]   per (row, 128-block) scale
   size_t partial;      // fp32  [routes_max, 7168]     weighted expert output per local route
+  size_t tile_ready;   // int32 [tiles_max]             GEMM1 column blocks of each tile whose C is stored
   size_t total;
   int tiles_max;
 };
@@ -399,6 +420,7 @@ inline Workspace make_workspace(int T, int E_local) {
   w.c_lo = take(tiles * IB * TILE_BYTES);
   w.c_scale = take(sizeof(float) * tiles * IB * TILE_M);
   w.partial = take(sizeof(float) * static_cast<size_t>(T) * kmax * H);
+  w.tile_ready = take(sizeof(int) * tiles);
   w.total = off;
   return w;
 }
