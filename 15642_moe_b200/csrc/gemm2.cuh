@@ -36,6 +36,7 @@ struct Gemm2Args {
   float* partial;           // [routes, 7168] dense: route (e, slot) is row dense_base[e] + slot
   int* dense_base;          // [E_local + 1] written by CTA 0 for the combine
   const int* tile_ready;    // [tiles] GEMM1 column blocks done per tile; a tile is read at G1_NT
+  int* unit_queue;          // zero at launch: the next unit to claim (dynamic schedule)
 };
 
 // Bounded wait until GEMM1 has stored all G1_NT column blocks of C for `tile` (acquire), then
@@ -65,9 +66,17 @@ constexpr int G2_THREADS = GEMM_THREADS;
 constexpr int G2_CTRL_BYTES = 4096;
 constexpr int G2_SMEM = G2_STAGES * G2_STAGE_BYTES + G2_CTRL_BYTES + 1024;
 
+// Units are claimed at run time from a global counter (tile-major order), so CTAs that start
+// early - on SMs GEMM1 has already left - take more of them. The producer claims and passes each
+// unit id to the MMA warp and the epilogue warps through a small ring in shared memory; -1 ends.
+constexpr int G2_UNIT_RING = 4;
+
 struct G2Ctrl {
   uint64_t full[G2_STAGES];
   uint64_t empty[G2_STAGES];
+  uint64_t ufull[G2_UNIT_RING];
+  uint64_t uempty[G2_UNIT_RING];
+  int unit[G2_UNIT_RING];
   uint64_t tfull[ACC_BUFS];
   uint64_t tempty[ACC_BUFS];
   uint64_t mma_done;
@@ -76,6 +85,20 @@ struct G2Ctrl {
   TileMap map;
 };
 static_assert(sizeof(G2Ctrl) <= G2_CTRL_BYTES, "control block too large");
+
+// Next unit id of this CTA's schedule (claim k), read by one thread (MMA) or one whole warp
+// (epilogue); -1 when the schedule is over or the CTA aborted.
+__device__ __forceinline__ int g2_next_unit(G2Ctrl* ctl, uint32_t k, volatile int* abort_flag, bool warp_wide) {
+  const int r = k % G2_UNIT_RING;
+  const uint32_t ph = (k / G2_UNIT_RING) & 1u;
+  const bool ok = warp_wide ? mbar_wait_warp(&ctl->ufull[r], ph, abort_flag, ST_TIMEOUT_EPILOGUE)
+                            : mbar_wait(&ctl->ufull[r], ph, abort_flag, ST_TIMEOUT_MMA);
+  if (!ok) return -1;
+  const int u = *static_cast<volatile int*>(&ctl->unit[r]);
+  if (warp_wide) __syncwarp();
+  if (!warp_wide || (threadIdx.x & 31) == 0) mbar_arrive(&ctl->uempty[r]);
+  return u;
+}
 
 __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __grid_constant__ Gemm2Args p) {
   extern __shared__ uint8_t smem_raw[];
@@ -100,6 +123,11 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
       mbar_init(&ctl->tfull[b], 1);
       mbar_init(&ctl->tempty[b], 8);
     }
+#pragma unroll
+    for (int r = 0; r < G2_UNIT_RING; ++r) {
+      mbar_init(&ctl->ufull[r], 1);
+      mbar_init(&ctl->uempty[r], 9);   // the MMA warp and the eight epilogue warps
+    }
     mbar_init(&ctl->mma_done, 1);
     ctl->abort_flag = 0;
     fence_mbar_init();
@@ -123,7 +151,15 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
       const uint64_t pol_w = policy_evict_first();
       uint32_t it = 0;
       int ready_tile = -1;
-      for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
+      for (uint32_t k = 0; !*abort_flag; ++k) {
+        // Claim the next unit and hand it to the MMA and epilogue warps.
+        int u = atomicAdd(p.unit_queue, 1);
+        if (u >= n_units) u = -1;
+        const int r = k % G2_UNIT_RING;
+        if (!mbar_wait(&ctl->uempty[r], ((k / G2_UNIT_RING) & 1u) ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) break;
+        ctl->unit[r] = u;
+        mbar_arrive(&ctl->ufull[r]);
+        if (u < 0) break;
         const int tile = u / G2_NT, nt = u % G2_NT;
         const int e = tile_expert(&ctl->map, p.E_local, tile);
         const size_t a_off = static_cast<size_t>(tile) * IB * TILE_BYTES;
@@ -169,7 +205,9 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
       constexpr uint32_t idesc = idesc_e4m3_f32(128, ACC_COLS);
       uint32_t it = 0;
       bool stop = false;
-      for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x) {
+      for (uint32_t k = 0; !stop; ++k) {
+        const int u = g2_next_unit(ctl, k, abort_flag, false);
+        if (u < 0) break;
         for (int ib = 0; ib < IB && !stop; ++ib, ++it) {
           const int s = it % G2_STAGES;
           const uint32_t ph = (it / G2_STAGES) & 1u;
@@ -214,7 +252,9 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
     const int row = q4 * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(q4 * 32) << 16;
     uint32_t it = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x) {
+    for (uint32_t k = 0;; ++k) {
+      const int u = g2_next_unit(ctl, k, abort_flag, true);
+      if (u < 0) break;
       const int tile = u / G2_NT, nt = u % G2_NT;
       const TileInfo ti = locate(&ctl->map, p.counts, p.E_local, tile, p.slots);
       const int e = ti.e;

@@ -310,7 +310,7 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   Gemm1Args g1{a_tiled, a_scale, static_cast<const uint8_t*>(w13_packed), w13_scale, counts, T,
                ws.tiles_max, E_local, c_hi, c_lo, c_scale, tile_ready};
   Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, counts, T,
-               ws.tiles_max, E_local, route_w, partial, dense_base, tile_ready};
+               ws.tiles_max, E_local, route_w, partial, dense_base, tile_ready, tile_ready + ws.tiles_max};
 
   auto mark = [&](int i) {
     if (events != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
@@ -409,7 +409,8 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
   Gemm1Args g1{a_tiled, a_scale, static_cast<const uint8_t*>(w13_packed), w13_scale, counts, L.r_cap,
                ws.tiles_max, L.e_rank, c_hi, c_lo, c_scale, tile_ready};
   Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, counts, L.r_cap,
-               ws.tiles_max, L.e_rank, ep_at<float>(me, L.route_w), partial, dense_base, tile_ready};
+               ws.tiles_max, L.e_rank, ep_at<float>(me, L.route_w), partial, dense_base, tile_ready,
+               tile_ready + ws.tiles_max};
   // Source side: local slot claims over all 256 experts (route_kernel with E_local = 256).
   int* local_counts = reinterpret_cast<int*>(W + sw.local_counts);
   int* reserve_base = reinterpret_cast<int*>(W + sw.base);

@@ -382,7 +382,8 @@ struct Workspace {
   size_t c_lo;         // u8    [tiles_max, 16, 128, 128] e4m3 residual
   size_t c_scale;      // fp32  [tiles_max, 16, 128]   per (row, 128-block) scale
   size_t partial;      // fp32  [routes_max, 7168]     weighted expert output per local route
-  size_t tile_ready;   // int32 [tiles_max]             GEMM1 column blocks of each tile whose C is stored
+  size_t tile_ready;   // int32 [tiles_max + 1]         GEMM1 column blocks of each tile whose C is stored;
+                       //                               the last entry is GEMM2's unit queue
   size_t total;
   int tiles_max;
 };
@@ -420,7 +421,7 @@ inline Workspace make_workspace(int T, int E_local) {
   w.c_lo = take(tiles * IB * TILE_BYTES);
   w.c_scale = take(sizeof(float) * tiles * IB * TILE_M);
   w.partial = take(sizeof(float) * static_cast<size_t>(T) * kmax * H);
-  w.tile_ready = take(sizeof(int) * tiles);
+  w.tile_ready = take(sizeof(int) * (tiles + 1));
   w.total = off;
   return w;
 }

@@ -216,9 +216,9 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__
                                                      float* __restrict__ a_scale,
                                                      int* __restrict__ tile_ready) {
   __shared__ TileMap map;
-  // The GEMM1 -> GEMM2 readiness counters of this call start at zero (GEMM1 runs after this
-  // kernel has completed).
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tiles_max; i += gridDim.x * blockDim.x) tile_ready[i] = 0;
+  // The GEMM1 -> GEMM2 readiness counters of this call and GEMM2's unit queue (entry
+  // tiles_max) start at zero (GEMM1 runs after this kernel has completed).
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i <= tiles_max; i += gridDim.x * blockDim.x) tile_ready[i] = 0;
   if (threadIdx.x < 32) build_tile_map(&map, counts, E_local, T, tiles_max);
   __syncthreads();
   const int routes = map.dense_off[E_local];
