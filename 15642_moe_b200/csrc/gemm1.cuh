@@ -165,11 +165,14 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
   uint8_t* smem = align_1024(smem_raw);
   G1Ctrl* ctl = reinterpret_cast<G1Ctrl*>(smem + G1_STAGES * G1_STAGE_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  // Launched programmatically after the gather: wait for it (and so for the router) before
+  // reading counts or tiles. Only then may GEMM2 be scheduled - as soon as every CTA of this grid
+  // has passed this point, so GEMM2 never sees the readiness counters before the gather zeroed
+  // them; it then waits per tile on tile_ready and never needs this grid to finish.
+  wait_prerequisite_grids();
+  if (threadIdx.x == 0) allow_dependent_launch();
   if (warp == 0) build_tile_map(&ctl->map, p.counts, p.E_local, p.slots, p.tiles_max);
   __syncthreads();
-  // GEMM2 may be scheduled on SMs as soon as every CTA of this grid is resident; it waits per
-  // tile on tile_ready, so it never needs this grid to finish.
-  if (threadIdx.x == 0) allow_dependent_launch();
   const int n_units = clamp_tiles(ctl->map.tile_off[p.E_local], p.tiles_max) * G1_NT;
   if (static_cast<int>(blockIdx.x) >= n_units) return;  // uniform per CTA, before any TMEM use
 

@@ -28,6 +28,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <utility>
 #include <string>
 
 using namespace moe;
@@ -148,18 +149,24 @@ int hidden_bf16_map(const void* hidden, int T, CUtensorMap* map) {
 // GEMM2 launched so that it may start on SMs that GEMM1's CTAs have left while GEMM1 still runs
 // (programmatic dependent launch; GEMM1 allows it once all its CTAs are resident, GEMM2 waits per
 // tile on the readiness counters GEMM1 publishes).
-cudaError_t launch_gemm2(const Gemm2Args& g2, int grid, cudaStream_t st) {
+template <typename... KArgs, typename... Args>
+cudaError_t launch_programmatic(void (*kernel)(KArgs...), int grid, int block, int smem, cudaStream_t st,
+                                Args&&... args) {
   cudaLaunchConfig_t cfg{};
   cfg.gridDim = dim3(static_cast<unsigned>(grid));
-  cfg.blockDim = dim3(G2_THREADS);
-  cfg.dynamicSmemBytes = G2_SMEM;
+  cfg.blockDim = dim3(static_cast<unsigned>(block));
+  cfg.dynamicSmemBytes = static_cast<size_t>(smem);
   cfg.stream = st;
   cudaLaunchAttribute attr[1];
   attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
   attr[0].val.programmaticStreamSerializationAllowed = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  return cudaLaunchKernelEx(&cfg, gemm2_weighted_kernel, g2);
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
+
+cudaError_t launch_gemm2(const Gemm2Args& g2, int grid, cudaStream_t st) {
+  return launch_programmatic(gemm2_weighted_kernel, grid, G2_THREADS, G2_SMEM, st, g2);
 }
 
 int grid_for(size_t work, int per_block, int cap) {
@@ -326,12 +333,20 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
                                               route_token, route_w);
   mark(1);
   const size_t route_max = static_cast<size_t>(T) * (E_local < TOP_K ? E_local : TOP_K);
-  gather_kernel<<<grid_for(route_max, 8, d->num_sms * 8), 256, 0, st>>>(
-      static_cast<const uint8_t*>(hidden), hidden_scale, T, counts, E_local, route_token,
-      ws.tiles_max, a_tiled, a_scale, tile_ready);
+  // gather and GEMM1 are launched programmatically: each may be scheduled while its predecessor
+  // finishes and waits for it in hardware before touching its results.
+  if (int rc = cuda_check(launch_programmatic(gather_kernel, grid_for(route_max, 8, d->num_sms * 8), 256, 0, st,
+                                              static_cast<const uint8_t*>(hidden), hidden_scale, T,
+                                              static_cast<const int*>(counts), E_local,
+                                              static_cast<const int*>(route_token), ws.tiles_max, a_tiled, a_scale,
+                                              tile_ready),
+                          "gather launch"))
+    return rc;
   mark(2);
   const int g1_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G1_NT, 1, d->num_sms);
-  gemm1_swiglu_kernel<<<g1_grid, G1_THREADS, G1_SMEM, st>>>(g1);
+  if (int rc = cuda_check(launch_programmatic(gemm1_swiglu_kernel, g1_grid, G1_THREADS, G1_SMEM, st, g1),
+                          "gemm1 launch"))
+    return rc;
   mark(3);
   const int g2_grid = grid_for(static_cast<size_t>(ws.tiles_max) * G2_NT, 1, d->num_sms);
   if (int rc = cuda_check(launch_gemm2(g2, g2_grid, st), "gemm2 launch")) return rc;

@@ -99,6 +99,11 @@ __device__ __forceinline__ void fence_proxy_async_global() {
 __device__ __forceinline__ void allow_dependent_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+// Wait until the grids this one depends on (the previous kernel of the stream) have completed and
+// their memory operations are visible; returns at once for a normally launched kernel.
+__device__ __forceinline__ void wait_prerequisite_grids() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
 
 // Routing metadata is produced on the device; a consumer never trusts it for addressing.
 __device__ __forceinline__ int clamp_tiles(int n, int tiles_max) {

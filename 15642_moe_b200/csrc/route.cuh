@@ -48,6 +48,9 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
                                                     int* __restrict__ token_route,
                                                     int* __restrict__ route_token,
                                                     float* __restrict__ route_w) {
+  // The gather kernel may be scheduled once every block of this grid runs; it waits for this
+  // grid's completion in hardware before reading anything written here.
+  if (threadIdx.x == 0) allow_dependent_launch();
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= T) return;
@@ -216,8 +219,12 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__
                                                      float* __restrict__ a_scale,
                                                      int* __restrict__ tile_ready) {
   __shared__ TileMap map;
+  // Launched programmatically after the router: wait for its results, then let GEMM1's CTAs be
+  // scheduled (GEMM1 waits for this grid in turn).
+  wait_prerequisite_grids();
+  if (threadIdx.x == 0) allow_dependent_launch();
   // The GEMM1 -> GEMM2 readiness counters of this call and GEMM2's unit queue (entry
-  // tiles_max) start at zero (GEMM1 runs after this kernel has completed).
+  // tiles_max) start at zero; GEMM1 waits for this grid to complete.
   for (int i = blockIdx.x * blockDim.x + threadIdx.x; i <= tiles_max; i += gridDim.x * blockDim.x) tile_ready[i] = 0;
   if (threadIdx.x < 32) build_tile_map(&map, counts, E_local, T, tiles_max);
   __syncthreads();
