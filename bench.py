@@ -480,6 +480,10 @@ def bench_ours(args, rank, world, local_rank, dist):
     # The reference benchmark's T list on one GPU, and configuration 2's tokens on every slice.
     sweep = t_sweep(pkg, inp, (step.w13p, step.w2p), device, peaks)
     spread = slice_spread(pkg, device, peaks)
+    # Configurations 3 and 4 as one GPU's layer (all 256 experts local): the N = 1 points of the
+    # expert-parallel strong-scaling curves reported by the N > 1 lines.
+    config3 = layer_1gpu(pkg, device, pkg.CONFIGS[3])
+    config4 = layer_1gpu(pkg, device, pkg.CONFIGS[4], steps=5)
 
     if rank != 0:
         return None
@@ -512,6 +516,8 @@ def bench_ours(args, rank, world, local_rank, dist):
                        "weight_bytes": int(layer_bytes),
                        "hbm_frac_layer": round(layer_bytes / (dms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
                        "roofline": droof, "stage_us": {k: round(v * 1e3, 2) for k, v in dstages.items()}},
+        "config3_layer": config3,
+        "config4_skew": config4,
         "t_sweep": sweep,
         "t1_probe": next(x for x in sweep if x["T"] == 1),
         "slices_t4096": spread,
@@ -560,6 +566,155 @@ def ep_routing_stats(pkg, inp, experts) -> dict:
                 max_per_expert=int(per.max()), tiles=int(((per + 127) // 128).sum()))
 
 
+class EpCase:
+    """One expert-parallel layer instance on this rank: `T_global` tokens of `cfg` split evenly
+    over the ranks, the experts `pool` placed e_rank per rank by expected load (route counts of a
+    calibration batch: seed+1 tokens routed with this layer's bias), packed weights of this
+    rank's experts, and an ExpertParallel context. Collective (every rank builds it)."""
+
+    def __init__(self, pkg, epm, rank, world, device, cfg, T_global, e_rank, pool):
+        self.pkg, self.epm, self.rank, self.world, self.dev = pkg, epm, rank, world, device
+        self.cfg, self.T_global, self.e_rank = cfg, T_global, e_rank
+        act = pkg.make_inputs(cfg.with_(T=T_global, E_local=1), device)
+        cal = pkg.make_inputs(cfg.with_(T=T_global, seed=cfg.seed + 1, E_local=1), device)["routing_logits"]
+        cidx, _ = pkg.route(cal, act["routing_bias"], cfg.routed_scaling_factor)
+        loads = torch.bincount(cidx.flatten().long(), minlength=256).cpu().numpy()
+        self.placement = epm.balanced_placement(loads, world, e_rank, experts=pool)
+        w = pkg.make_weights(cfg, self.placement[rank], device)
+        idx, _ = pkg.route(act["routing_logits"], act["routing_bias"], cfg.routed_scaling_factor)
+        per = np.bincount(idx.cpu().numpy().ravel(), minlength=256)[list(self.placement[rank])]
+        self.routes, self.active = int(per.sum()), int((per > 0).sum())
+        self.lo, self.hi = epm.token_range(T_global, world, rank)
+        lo, hi = self.lo, self.hi
+        self.k = dict(hidden=act["hidden_states"][lo:hi].contiguous(),
+                      hs=act["hidden_states_scale"][:, lo:hi].float().contiguous(),
+                      lg=act["routing_logits"][lo:hi].float().contiguous(),
+                      b=act["routing_bias"].float().reshape(-1).contiguous(),
+                      s13=w["gemm1_weights_scale"].float().contiguous(),
+                      s2=w["gemm2_weights_scale"].float().contiguous())
+        self.w13p, self.w2p = pkg.pack_w13(w["gemm1_weights"]), pkg.pack_w2(w["gemm2_weights"])
+        del w, cal, act
+        self.out = torch.empty((hi - lo, 7168), dtype=torch.bfloat16, device=device)
+        self.ctx = epm.ExpertParallel(t_rank_max=max(1, hi - lo), e_rank=e_rank, device=device,
+                                      placement=self.placement)
+
+    def __call__(self, events=None, out=None):
+        k = self.k
+        return self.ctx.forward(k["hidden"], k["hs"], self.w13p, k["s13"], self.w2p, k["s2"], k["lg"], k["b"],
+                                float(self.cfg.routed_scaling_factor), out=self.out if out is None else out,
+                                events=events)
+
+    def close(self):
+        self.ctx.close()
+
+    def time_ms(self, dist, steps: int, warmup: int) -> float:
+        """Max over ranks of the device time of one forward, from `steps` timed after `warmup`."""
+        for _ in range(warmup):
+            self()
+        torch.cuda.synchronize()
+        dist.barrier()
+        torch.cuda.synchronize()
+        ms = time_steps(self, steps)
+        t = torch.tensor([ms], device=self.dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        return float(t.item()) / steps
+
+    def parity(self, dist, oracle_rows: int = 8) -> dict:
+        """This rank's output against (1) the same layer composed from single-expert forwards on
+        this GPU - per owner d ascending, the fp32 chain over d's experts in ascending order of
+        moe_forward(..., fp32_out=True) with that one expert, then the fp32 chain over owners,
+        rounded once - bit for bit; (2) on rank 0, the CPU oracle (single rounding over all the
+        token's experts, reference tolerance) on a few rows. Collective."""
+        pkg, k = self.pkg, self.k
+        got = self().clone()
+        torch.cuda.synchronize()
+        status = pkg.device_status(reset=True)
+        T_r = self.hi - self.lo
+        acc = torch.zeros((T_r, 7168), dtype=torch.float32, device=self.dev)
+        for d in range(self.world):
+            part = torch.zeros_like(acc)
+            for g in sorted(self.placement[d]):
+                w = pkg.make_weights(self.cfg, [g], self.dev)
+                if T_r:
+                    part += pkg.moe_forward(k["hidden"], k["hs"], pkg.pack_w13(w["gemm1_weights"]),
+                                            w["gemm1_weights_scale"].float().contiguous(),
+                                            pkg.pack_w2(w["gemm2_weights"]),
+                                            w["gemm2_weights_scale"].float().contiguous(), k["lg"], k["b"],
+                                            float(self.cfg.routed_scaling_factor), g, fp32_out=True)
+            acc += part
+        ref = acc.to(torch.bfloat16)
+        differ = int((got.view(torch.int16) != ref.view(torch.int16)).sum().item())
+        res = {"rows": T_r, "bf16_values_differing_from_composition": differ, "device_status": status}
+        if self.rank == 0 and T_r:
+            res["oracle"] = self._oracle_rows(got, oracle_rows)
+        flags = torch.tensor([float(differ != 0 or status != 0), float(res.get("oracle", {}).get("bad", 0) > 0)],
+                             device=self.dev)
+        dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+        res["all_ranks_bit_exact"] = bool(flags[0].item() == 0)
+        res["ok"] = bool(flags[0].item() == 0 and flags[1].item() == 0)
+        return res
+
+    def _oracle_rows(self, got, n: int) -> dict:
+        from oracle import moe_oracle as O
+        pkg, k, cfg = self.pkg, self.k, self.cfg
+        lg = k["lg"].cpu().numpy()
+        idx, _ = O.route(lg, k["b"].cpu().numpy(), cfg.routed_scaling_factor)
+        pool = {int(g) for p in self.placement for g in p}
+        rows = [t for t in range(idx.shape[0]) if any(int(g) in pool for g in idx[t])][:n]
+        sub = dict(routing_logits=lg[rows], routing_bias=k["b"].cpu().numpy(),
+                   hidden_states=k["hidden"][rows].view(torch.uint8).cpu().numpy(),
+                   hidden_states_scale=np.ascontiguousarray(k["hs"][:, rows].cpu().numpy()),
+                   local_expert_offset=0, routed_scaling_factor=cfg.routed_scaling_factor)
+        out = np.zeros((len(rows), 7168), np.float32)
+        for g in sorted({int(g) for t in rows for g in idx[t]} & pool):
+            w = pkg.make_weights(cfg, [g], self.dev)
+            one = dict(sub, local_expert_offset=g,
+                       gemm1_weights=w["gemm1_weights"].view(torch.uint8).cpu().numpy(),
+                       gemm1_weights_scale=w["gemm1_weights_scale"].cpu().numpy(),
+                       gemm2_weights=w["gemm2_weights"].view(torch.uint8).cpu().numpy(),
+                       gemm2_weights_scale=w["gemm2_weights_scale"].cpu().numpy())
+            out = O.moe_forward(**one, accumulate=out, return_fp32=True)
+        ref = O.f32_to_bf16_bits(out)
+        r = O.check_tolerance(ref, got[rows].view(torch.int16).cpu().numpy().view(np.uint16))
+        r["rows"] = len(rows)
+        return r
+
+
+def ep_layer_measure(pkg, epm, dist, rank, world, device, cfg, T_global, e_rank, pool, steps, warmup,
+                     what: str) -> dict:
+    """Layer tokens/s of one expert-parallel configuration (max over ranks), with its parity."""
+    case = EpCase(pkg, epm, rank, world, device, cfg, T_global, e_rank, pool)
+    try:
+        par = case.parity(dist, oracle_rows=4)
+        ms = case.time_ms(dist, steps, warmup)
+        rt = torch.tensor([case.routes], device=device, dtype=torch.float64)
+        parts = [torch.empty_like(rt) for _ in range(world)]
+        dist.all_gather(parts, rt)
+    finally:
+        case.close()
+    return {"what": what, "T_global": T_global, "experts_per_rank": e_rank, "experts": len(pool),
+            "us_per_layer": round(ms * 1e3, 2), "layer_tokens_per_s": round(T_global / (ms * 1e-3), 1),
+            "routes_per_rank": [int(p.item()) for p in parts], "parity": par, "steps": steps}
+
+
+def layer_1gpu(pkg, device, cfg, steps: int = 10) -> dict:
+    """Configuration 3 (or 4) on one GPU: the full 256-expert layer (moe_forward with all 256
+    experts local; the N = 1 point of the expert-parallel strong-scaling curve)."""
+    inp = pkg.make_inputs(cfg, device)
+    step = Step(pkg, inp, device)
+    rs = routing_stats(pkg, inp)
+    del inp["gemm1_weights"], inp["gemm2_weights"]
+    for _ in range(2):
+        step()
+    us = time_steps(step, steps) / steps * 1e3
+    del step
+    torch.cuda.empty_cache()
+    return {"what": f"{cfg.name}: full 256-expert layer, T={cfg.T}, one GPU (all experts local)",
+            "T_global": cfg.T, "experts_per_rank": 256, "experts": 256, "us_per_layer": round(us, 2),
+            "layer_tokens_per_s": round(cfg.T / (us * 1e-6), 1), "routes_per_rank": [rs["routes"]],
+            "steps": steps}
+
+
 def bench_ep(args, rank, world, local_rank, dist):
     """Expert-parallel layer over `world` GPUs (weak scaling of configuration 2's per-GPU work).
 
@@ -576,32 +731,18 @@ def bench_ep(args, rank, world, local_rank, dist):
     torch.cuda.set_device(device)
     peaks = load_peaks()
     e_rank, T_global = 32, pkg.CONFIGS[2].T
-    cfg = pkg.CONFIGS[2].with_(local_expert_offset=e_rank * rank)
-    inp = pkg.make_inputs(cfg.with_(E_local=1), device)
-    # Expert placement balanced by expected load: the route counts of a calibration batch (other
-    # tokens, seed 1, routed with this layer's bias) over the instantiated experts 0 .. 32N-1.
-    cal = pkg.make_inputs(cfg.with_(seed=1, E_local=1), device)["routing_logits"]
-    cidx, _ = pkg.route(cal, inp["routing_bias"], cfg.routed_scaling_factor)
-    loads = torch.bincount(cidx.flatten().long(), minlength=256).cpu().numpy()
-    placement = epm.balanced_placement(loads, world, e_rank, experts=range(e_rank * world))
-    inp.update(pkg.make_weights(cfg, placement[rank], device))
-    rs = ep_routing_stats(pkg, inp, placement[rank])
-    lo, hi = epm.token_range(T_global, world, rank)
-    mine = dict(inp)
-    mine["hidden_states"] = inp["hidden_states"][lo:hi].contiguous()
-    mine["hidden_states_scale"] = inp["hidden_states_scale"][:, lo:hi].contiguous()
-    mine["routing_logits"] = inp["routing_logits"][lo:hi].contiguous()
+    cfg = pkg.CONFIGS[2]
+    case = EpCase(pkg, epm, rank, world, device, cfg, T_global, e_rank, range(e_rank * world))
+    placement, ctx, k, w13p, w2p, out = case.placement, case.ctx, case.k, case.w13p, case.w2p, case.out
+    rs = {"routes": case.routes, "active": case.active, "max_per_expert": 0, "tiles": 0}
+    lo, hi = case.lo, case.hi
     T_r = hi - lo
-    w13p, w2p = pkg.pack_w13(inp["gemm1_weights"]), pkg.pack_w2(inp["gemm2_weights"])
-    k = dict(hidden=mine["hidden_states"], hs=mine["hidden_states_scale"].float().contiguous(),
-             s13=inp["gemm1_weights_scale"].float().contiguous(), s2=inp["gemm2_weights_scale"].float().contiguous(),
-             lg=mine["routing_logits"].float().contiguous(), b=inp["routing_bias"].float().reshape(-1).contiguous())
-    out = torch.empty((T_r, 7168), dtype=torch.bfloat16, device=device)
-    ctx = epm.ExpertParallel(t_rank_max=T_r, e_rank=e_rank, device=device, placement=placement)
+    mine = {"hidden_states": k["hidden"], "hidden_states_scale": k["hs"], "routing_logits": k["lg"]}
+    # Output parity of this very configuration before anything is timed.
+    parity = case.parity(dist)
 
     def step(events=None):
-        ctx.forward(k["hidden"], k["hs"], w13p, k["s13"], w2p, k["s2"], k["lg"], k["b"],
-                    float(cfg.routed_scaling_factor), out=out, events=events)
+        case(events=events)
 
     try:
         for _ in range(args.warmup):
@@ -666,6 +807,18 @@ def bench_ep(args, rank, world, local_rank, dist):
         dist.all_reduce(routes_all)
     finally:
         ctx.close()
+    # The model's layer at this N (strong scaling): configuration 3, and configuration 4's skewed
+    # routing; each checked for parity like the headline case before it is timed.
+    del case
+    torch.cuda.empty_cache()
+    c3, c4 = pkg.CONFIGS[3], pkg.CONFIGS[4]
+    config3 = ep_layer_measure(pkg, epm, dist, rank, world, device, c3, c3.T, 256 // world, range(256), 10, 3,
+                               "config 3: full 256-expert layer, T=8192 split evenly over the ranks, 256/N "
+                               "experts per rank (placement balanced by a calibration batch)")
+    torch.cuda.empty_cache()
+    config4 = ep_layer_measure(pkg, epm, dist, rank, world, device, c4, c4.T, 256 // world, range(256), 5, 2,
+                               "config 4: skewed routing (bias +1.5 on 2 experts per group), T=16384 split "
+                               "evenly, 256/N experts per rank (placement balanced by a calibration batch)")
     if rank != 0:
         return None
     slices = T_global * world
@@ -687,6 +840,9 @@ def bench_ep(args, rank, world, local_rank, dist):
         "routing": {"T_per_rank": T_r, "routes_all_ranks": int(routes_all.item()), "routes_rank0": rs["routes"],
                     "active_experts_rank0": rs["active"]},
         "layer_tokens_per_s": round(T_global * args.steps / (ms * 1e-3), 1),
+        "parity": parity,
+        "config3_layer": config3,
+        "config4_skew": config4,
         "roofline": roof,
         "stage_us_rank0": {kk: round(v * 1e3, 2) for kk, v in stages.items()},
         "routes_per_rank": [int(p[0]) for p in per_rank],
