@@ -250,6 +250,10 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __grid_constant_
 // second reads it, so no host value is baked into the launches.
 __global__ void __launch_bounds__(32) ep_barrier_kernel(const __grid_constant__ EpPeers peers, size_t flag_off,
                                                         size_t epoch_off, int rank, int world, int advance) {
+  // May be launched programmatically: everything the previous kernel stored must be complete
+  // before this rank signals. The next kernel may then be scheduled (it waits for this one).
+  wait_prerequisite_grids();
+  allow_dependent_launch();
   const int lane = threadIdx.x;
   unsigned* ep = ep_at<unsigned>(peers.base[rank], epoch_off);
   unsigned epoch = 0;
@@ -327,6 +331,7 @@ __global__ void __launch_bounds__(COMBINE_THREADS) ep_final_combine_kernel(const
                                                                            EpLayout L, int T,
                                                                            const int* __restrict__ topk_idx,
                                                                            __nv_bfloat16* __restrict__ out) {
+  wait_prerequisite_grids();                // launched programmatically after the done barrier
   const int t = blockIdx.x;
   if (t >= T) return;
   const int tid = threadIdx.x;

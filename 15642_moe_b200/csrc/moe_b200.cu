@@ -453,11 +453,20 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
   ep_barrier_kernel<<<1, 32, 0, st>>>(c->peers, L.arrive, L.epoch, c->rank, L.world, 1);
   mark(3);
   const size_t route_max = static_cast<size_t>(L.r_cap) * (L.e_rank < TOP_K ? L.e_rank : TOP_K);
-  gather_kernel<<<grid_for(route_max, 8, d->num_sms * 8), 256, 0, st>>>(
-      me + L.recv_rows, ep_at<float>(me, L.recv_scale), L.r_cap, counts, L.e_rank,
-      ep_at<int>(me, L.route_token), ws.tiles_max, a_tiled, a_scale, tile_ready);
+  if (int rc = cuda_check(launch_programmatic(gather_kernel, grid_for(route_max, 8, d->num_sms * 8), 256, 0, st,
+                                              static_cast<const uint8_t*>(me + L.recv_rows),
+                                              static_cast<const float*>(ep_at<float>(me, L.recv_scale)), L.r_cap,
+                                              static_cast<const int*>(counts), L.e_rank,
+                                              static_cast<const int*>(ep_at<int>(me, L.route_token)), ws.tiles_max,
+                                              a_tiled, a_scale, tile_ready),
+                          "gather launch"))
+    return rc;
   mark(4);
-  gemm1_swiglu_kernel<<<grid_for(static_cast<size_t>(ws.tiles_max) * G1_NT, 1, d->num_sms), G1_THREADS, G1_SMEM, st>>>(g1);
+  if (int rc = cuda_check(launch_programmatic(gemm1_swiglu_kernel,
+                                              grid_for(static_cast<size_t>(ws.tiles_max) * G1_NT, 1, d->num_sms),
+                                              G1_THREADS, G1_SMEM, st, g1),
+                          "gemm1 launch"))
+    return rc;
   mark(5);
   if (int rc = cuda_check(launch_gemm2(g2, grid_for(static_cast<size_t>(ws.tiles_max) * G2_NT, 1, d->num_sms), st),
                           "gemm2 launch"))
@@ -470,7 +479,12 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
   ep_barrier_kernel<<<1, 32, 0, st>>>(c->peers, L.done, L.epoch, c->rank, L.world, 0);
   mark(8);
   if (T > 0)
-    ep_final_combine_kernel<<<T, COMBINE_THREADS, 0, st>>>(me, L, T, topk_idx, static_cast<__nv_bfloat16*>(out_bf16));
+    if (int rc = cuda_check(launch_programmatic(ep_final_combine_kernel, T, COMBINE_THREADS, 0, st,
+                                                static_cast<const uint8_t*>(me), L, T,
+                                                static_cast<const int*>(topk_idx),
+                                                static_cast<__nv_bfloat16*>(out_bf16)),
+                            "final combine launch"))
+      return rc;
   mark(9);
   return cuda_check(cudaGetLastError(), "moe_ep_forward launch");
 }

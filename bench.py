@@ -931,6 +931,18 @@ def bench_reference(args, rank, world):
                     "d2h_bytes_per_step": 0}}
 
 
+def profile_forwards(T: int, n: int = 4) -> None:
+    """n forwards of configuration 2's experts on T tokens: input synthesis (5 launches), weight
+    packing (2), then 5 kernels per forward."""
+    pkg = importlib.import_module("15642_moe_b200")
+    inp = pkg.make_inputs(pkg.CONFIGS[2].with_(T=T), "cuda")
+    step = Step(pkg, inp, torch.device("cuda"))
+    for _ in range(n):
+        step()
+    torch.cuda.synchronize()
+    print("profile_forwards", T, "device status", pkg.device_status(reset=True), file=sys.stderr)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -939,7 +951,13 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--burn-in", type=float, default=2.0, help="untimed seconds before timing")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--profile-forwards", type=int, default=0, metavar="T",
+                    help="profiling driver: run 4 forwards of configuration 2's weights with T tokens "
+                         "(seed 0) and exit without timing (for ncu launch lists and captures)")
     args = ap.parse_args()
+    if args.profile_forwards:
+        profile_forwards(args.profile_forwards)
+        return
     args.warmup = max(args.warmup, 3)
     # Standard output carries the one JSON line only: keep a handle on it, then send whatever
     # else writes to file descriptor 1 (NCCL's version banner, library prints) to stderr.
