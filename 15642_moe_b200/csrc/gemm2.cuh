@@ -33,7 +33,7 @@ struct Gemm2Args {
   int tiles_max;            // capacity of the c_* tile arrays
   int E_local;
   const float* route_w;     // [E_local, slots] routing weight of each expert slot
-  float* partial;           // [routes, 7168] dense: route (e, slot) is row dense_base[e] + slot
+  float* partial;           // route (e, slot) is dense row dense_base[e] + slot (partial_offset layout)
   int* dense_base;          // [E_local + 1] written by CTA 0 for the combine
   const int* tile_ready;    // [tiles] GEMM1 column blocks done per tile; a tile is read at G1_NT
   int* unit_queue;          // zero at launch: the next unit to claim (dynamic schedule)
@@ -285,14 +285,16 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
       if (row < ti.rows) {
         const int slot = ti.m * TILE_M + row;
         const float w = p.route_w[static_cast<size_t>(e) * p.slots + slot];
-        float* base = p.partial + static_cast<size_t>(ctl->map.dense_off[e] + slot) * H + nt * 256 + hf * 64;
+        const size_t d = static_cast<size_t>(ctl->map.dense_off[e] + slot);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
-          float4* dst = reinterpret_cast<float4*>(base + h * 128);
 #pragma unroll
-          for (int i = 0; i < 16; ++i)
-            dst[i] = make_float4(acc[h * 64 + 4 * i] * w, acc[h * 64 + 4 * i + 1] * w,
-                                 acc[h * 64 + 4 * i + 2] * w, acc[h * 64 + 4 * i + 3] * w);
+          for (int g = 0; g < 8; ++g) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = acc[h * 64 + 8 * g + i] * w;
+            st_global_v8(p.partial + partial_offset(d, nt * 256 + h * 128 + hf * 64 + 8 * g), v);
+          }
         }
       }
     }

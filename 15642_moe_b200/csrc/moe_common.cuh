@@ -386,7 +386,8 @@ struct Workspace {
   size_t c_hi;         // u8    [tiles_max, 16, 128, 128] SwiGLU output, e4m3 high part
   size_t c_lo;         // u8    [tiles_max, 16, 128, 128] e4m3 residual
   size_t c_scale;      // fp32  [tiles_max, 16, 128]   per (row, 128-block) scale
-  size_t partial;      // fp32  [routes_max, 7168]     weighted expert output per local route
+  size_t partial;      // fp32  [routes_max / 128, 224, 128, 32] weighted expert output per local route,
+                       //       route d's 32-column group g at partial_offset(d, 32 g)
   size_t tile_ready;   // int32 [tiles_max + 1]         GEMM1 column blocks of each tile whose C is stored;
                        //                               the last entry is GEMM2's unit queue
   size_t total;
@@ -425,10 +426,26 @@ inline Workspace make_workspace(int T, int E_local) {
   w.c_hi = take(tiles * IB * TILE_BYTES);
   w.c_lo = take(tiles * IB * TILE_BYTES);
   w.c_scale = take(sizeof(float) * tiles * IB * TILE_M);
-  w.partial = take(sizeof(float) * static_cast<size_t>(T) * kmax * H);
+  w.partial = take(sizeof(float) * ((static_cast<size_t>(T) * kmax + TILE_M - 1) / TILE_M) * TILE_M * H);
   w.tile_ready = take(sizeof(int) * (tiles + 1));
   w.total = off;
   return w;
+}
+
+// Layout of the weighted per-route rows (GEMM2 -> combine): dense route rows in blocks of 128, each
+// block stored as 224 column groups of [128 rows][32 floats]. GEMM2's epilogue (one row per thread)
+// writes each 128-byte group with four full-sector 256-bit stores, and the combine reads a row's
+// group as one whole 128-byte line.
+constexpr int PART_G = H / 32;
+__host__ __device__ __forceinline__ size_t partial_offset(size_t d, int col) {
+  return ((d / TILE_M * PART_G + static_cast<size_t>(col >> 5)) * TILE_M + d % TILE_M) * 32 + (col & 31);
+}
+
+// 8 consecutive fp32 values to global memory in one 256-bit store (32-byte aligned address).
+__device__ __forceinline__ void st_global_v8(float* p, const float* v) {
+  asm volatile("st.global.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]),
+               "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])
+               : "memory");
 }
 
 // ------------------------------------------------------------------------------------------

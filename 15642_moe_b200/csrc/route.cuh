@@ -280,7 +280,8 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
 constexpr int COMBINE_Q = H / 4 / COMBINE_THREADS;  // 4 float4 groups per thread
 
 // Adds a token's weighted expert outputs to acc: `routes` holds n entries (le << 16) | slot in
-// ascending le, and route (le, slot) is row dense_base[le] + slot of `partial` (dense_base
+// ascending le, and route (le, slot) is dense row dense_base[le] + slot of `partial` (layout of
+// partial_offset; dense_base
 // written by the GEMM2 kernel, entry [E_local] = all routes). Each entry is checked against the
 // expert's row range before it addresses anything.
 __device__ __forceinline__ void add_routes(float (&acc)[16], const float* __restrict__ partial,
@@ -300,10 +301,11 @@ __device__ __forceinline__ void add_routes(float (&acc)[16], const float* __rest
         report_status(ST_BAD_INDEX);
         continue;
       }
-      const float4* src = reinterpret_cast<const float4*>(partial + static_cast<size_t>(row) * H) + tid;
       float4 p[COMBINE_Q];
 #pragma unroll
-      for (int j = 0; j < COMBINE_Q; ++j) p[j] = __ldcs(src + j * COMBINE_THREADS);
+      for (int j = 0; j < COMBINE_Q; ++j)
+        p[j] = __ldcs(reinterpret_cast<const float4*>(partial + partial_offset(static_cast<size_t>(row),
+                                                                               4 * (tid + j * COMBINE_THREADS))));
 #pragma unroll
       for (int j = 0; j < COMBINE_Q; ++j) {
         acc[4 * j + 0] = __fadd_rn(acc[4 * j + 0], p[j].x);

@@ -159,7 +159,10 @@ def test_stages(pkg, oracle):
     cval = (oracle.decode_e4m3(hi) + oracle.decode_e4m3(lo)) * cs[..., None]
     cval = cval.transpose(0, 2, 1, 3).reshape(n_tiles * 128, 2048)
     routes = int(exp_counts.sum())
-    partial = region(ws, lay, "partial", torch.float32, routes * 7168).reshape(routes, 7168)
+    # weighted route rows: dense rows in blocks of 128, each block as [224 column groups][128 rows][32]
+    nblk = (routes + 127) // 128
+    partial = (region(ws, lay, "partial", torch.float32, nblk * 128 * 7168).reshape(nblk, 224, 128, 32)
+               .transpose(0, 2, 1, 3).reshape(nblk * 128, 7168))
     t0 = 0
     worst_c, worst_o = 0.0, 0.0
     for e in range(E):
