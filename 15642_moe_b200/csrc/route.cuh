@@ -167,26 +167,32 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
     const int le = sel_idx[k] - local_offset;
     nlocal += (le >= 0 && le < E_local) ? 1 : 0;
   }
+  // Lane k < 8 handles pick k: all eight slot claims (atomics) and stores of a token are in
+  // flight together rather than one after another.
+  if (lane < TOP_K) {
+    int my_idx = sel_idx[0];
+    float my_s = sel_s[0];
 #pragma unroll
-  for (int k = 0; k < TOP_K; ++k) {
-    if (lane == k) {
-      const float w = __fmul_rn(__fdiv_rn(sel_s[k], wsum), rsf);
-      topk_idx[static_cast<size_t>(t) * TOP_K + k] = sel_idx[k];
-      topk_w[static_cast<size_t>(t) * TOP_K + k] = w;
-      const int le = sel_idx[k] - local_offset;
-      if (counts != nullptr && le >= 0 && le < E_local) {
-        const int slot = atomicAdd(&counts[le], 1);
-        route_token[static_cast<size_t>(le) * T + slot] = t;
-        route_w[static_cast<size_t>(le) * T + slot] = w;
-        // Position in the token's list: local picks with a lower expert id come first.
-        int pos = 0;
+    for (int k = 1; k < TOP_K; ++k) {
+      my_idx = lane == k ? sel_idx[k] : my_idx;
+      my_s = lane == k ? sel_s[k] : my_s;
+    }
+    const float w = __fmul_rn(__fdiv_rn(my_s, wsum), rsf);
+    topk_idx[static_cast<size_t>(t) * TOP_K + lane] = my_idx;
+    topk_w[static_cast<size_t>(t) * TOP_K + lane] = w;
+    const int le = my_idx - local_offset;
+    if (counts != nullptr && le >= 0 && le < E_local) {
+      const int slot = atomicAdd(&counts[le], 1);
+      route_token[static_cast<size_t>(le) * T + slot] = t;
+      route_w[static_cast<size_t>(le) * T + slot] = w;
+      // Position in the token's list: local picks with a lower expert id come first.
+      int pos = 0;
 #pragma unroll
-        for (int j = 0; j < TOP_K; ++j) {
-          const int lj = sel_idx[j] - local_offset;
-          pos += (lj >= 0 && lj < le) ? 1 : 0;
-        }
-        token_route[static_cast<size_t>(t) * TOP_K + pos] = (le << 16) | slot;
+      for (int j = 0; j < TOP_K; ++j) {
+        const int lj = sel_idx[j] - local_offset;
+        pos += (lj >= 0 && lj < le) ? 1 : 0;
       }
+      token_route[static_cast<size_t>(t) * TOP_K + pos] = (le << 16) | slot;
     }
   }
   if (lane == 0 && token_nr != nullptr) token_nr[t] = nlocal;
