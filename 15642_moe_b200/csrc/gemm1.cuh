@@ -48,6 +48,7 @@ constexpr int G1_STAGE_BYTES = G1_A_BYTES + G1_B_BYTES;
 constexpr int G1_THREADS = GEMM_THREADS;
 constexpr int G1_CTRL_BYTES = 8192;
 constexpr int G1_SMEM = G1_STAGES * G1_STAGE_BYTES + G1_CTRL_BYTES + 1024;
+static_assert(G1_STAGES <= HB, "the first unit fills every stage");
 // TMEM accumulators: a 256-column unit is computed per 128-K block as ACC_SPLIT MMA groups of
 // N = ACC_COLS, each into its own accumulator; all 512 TMEM columns rotate as ACC_BUFS
 // accumulators, so ACC_BUFS / ACC_SPLIT K blocks can be in flight at once.
@@ -165,12 +166,13 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
   uint8_t* smem = align_1024(smem_raw);
   G1Ctrl* ctl = reinterpret_cast<G1Ctrl*>(smem + G1_STAGES * G1_STAGE_BYTES);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // Launched programmatically after the gather: wait for it (and so for the router) before
-  // reading counts or tiles. Only then may GEMM2 be scheduled - as soon as every CTA of this grid
-  // has passed this point, so GEMM2 never sees the readiness counters before the gather zeroed
+  // Launched programmatically after the gather, which lets this grid be scheduled only after its
+  // own wait for the router's completion: the per-expert counts are final here, so every unit's
+  // expert (and weight tiles) is known before the gathered rows are. The producer starts the
+  // first unit's weight reads, then waits for the gather (below); every other thread waits before
+  // its first read of the gather's output. GEMM2 may be scheduled once every CTA of this grid has
+  // passed thread 0's wait, so it never sees the readiness counters before the gather zeroed
   // them; it then waits per tile on tile_ready and never needs this grid to finish.
-  wait_prerequisite_grids();
-  if (threadIdx.x == 0) allow_dependent_launch();
   if (warp == 0) build_tile_map(&ctl->map, p.counts, p.E_local, p.slots, p.tiles_max);
   __syncthreads();
   const int n_units = clamp_tiles(ctl->map.tile_off[p.E_local], p.tiles_max) * G1_NT;
@@ -200,6 +202,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
   tc_fence_after();
   const uint32_t tmem = ctl->tmem_base;
   volatile int* abort_flag = &ctl->abort_flag;
+  if (threadIdx.x != 0) wait_prerequisite_grids();
 
   if (warp < 4) {
     regs_dec<REGS_CTRL>();
@@ -208,13 +211,35 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
-      uint32_t it = 0;
+      // First unit (blockIdx.x < n_units): while the gather still runs, fill every stage with its
+      // weight tile, so HBM is busy before the first row tile exists. Then wait for the gather,
+      // let GEMM2 be scheduled, and complete the stages with their row tiles. (Pulling further
+      // weight tiles into L2 with bulk prefetches at this point was measured slower.)
+      {
+        const int tile = blockIdx.x / G1_NT, j = blockIdx.x % G1_NT;
+        const int e = tile_expert(&ctl->map, p.E_local, tile);
+        const uint8_t* b_src = p.w13p + (static_cast<size_t>(e) * G1_NT + j) * HB * G1_B_BYTES;
+#pragma unroll
+        for (int s = 0; s < G1_STAGES; ++s) {
+          mbar_arrive_expect_tx(&ctl->full[s], G1_STAGE_BYTES);
+          bulk_g2s_hint(smem + s * G1_STAGE_BYTES + G1_A_BYTES, b_src + static_cast<size_t>(s) * G1_B_BYTES,
+                        G1_B_BYTES, &ctl->full[s], pol_w);
+        }
+        wait_prerequisite_grids();
+        allow_dependent_launch();
+        const uint8_t* a_src = p.a_tiled + static_cast<size_t>(tile) * HB * TILE_BYTES;
+#pragma unroll
+        for (int s = 0; s < G1_STAGES; ++s)
+          bulk_g2s(smem + s * G1_STAGE_BYTES, a_src + static_cast<size_t>(s) * TILE_BYTES, G1_A_BYTES,
+                   &ctl->full[s]);
+      }
+      uint32_t it = G1_STAGES;
       for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
         const int tile = u / G1_NT, j = u % G1_NT;
         const int e = tile_expert(&ctl->map, p.E_local, tile);
         const uint8_t* a_src = p.a_tiled + static_cast<size_t>(tile) * HB * TILE_BYTES;
         const uint8_t* b_src = p.w13p + (static_cast<size_t>(e) * G1_NT + j) * HB * G1_B_BYTES;
-        for (int kb = 0; kb < HB; ++kb, ++it) {
+        for (int kb = u == static_cast<int>(blockIdx.x) ? G1_STAGES : 0; kb < HB; ++kb, ++it) {
           const int s = it % G1_STAGES;
           const uint32_t ph = (it / G1_STAGES) & 1u;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) break;
