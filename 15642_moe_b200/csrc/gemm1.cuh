@@ -46,7 +46,14 @@ constexpr int G1_A_BYTES = TILE_BYTES;
 constexpr int G1_B_BYTES = 2 * TILE_BYTES;
 constexpr int G1_STAGE_BYTES = G1_A_BYTES + G1_B_BYTES;
 constexpr int G1_THREADS = GEMM_THREADS;
-constexpr int G1_CTRL_BYTES = 8192;
+constexpr int G1_CTRL_BYTES = 20480;
+// Block scales reach the epilogue through shared memory, copied by the producer ahead of the
+// stages: the rows' scales a_scale[tile, kb, 0..127] for G1_SC_KB consecutive K blocks per copy,
+// in a ring of G1_SC_RING slots, and W13's 2 x 56 scales once per unit (two slots by unit
+// parity). Loading them from global memory in the epilogue stalled it on every K block.
+constexpr int G1_SC_KB = 8;
+constexpr int G1_SC_RING = 3;
+static_assert(HB % G1_SC_KB == 0, "a unit's K blocks form whole scale groups");
 constexpr int G1_SMEM = G1_STAGES * G1_STAGE_BYTES + G1_CTRL_BYTES + 1024;
 static_assert(G1_STAGES <= HB, "the first unit fills every stage");
 // TMEM accumulators: a 256-column unit is computed per 128-K block as ACC_SPLIT MMA groups of
@@ -65,10 +72,16 @@ struct G1Ctrl {
   uint64_t empty[G1_STAGES];
   uint64_t tfull[ACC_BUFS];
   uint64_t tempty[ACC_BUFS];
+  uint64_t sfull[G1_SC_RING];    // row scales of scale group g landed (slot g % G1_SC_RING)
+  uint64_t sempty[G1_SC_RING];   // ... and read by the eight epilogue warps
+  uint64_t ufull[2];             // W13 scales of the unit with this parity landed
+  uint64_t uempty[2];            // ... and read
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
   float amax[2][2][TILE_M];  // [unit parity][column half][row]
+  alignas(16) float a_sc[G1_SC_RING][G1_SC_KB][TILE_M];   // a_scale[tile, kb, :] of a group
+  alignas(16) float w_sc[2][2][HB];             // [unit parity][X1, X2][kb] of W13
   TileMap map;
 };
 static_assert(sizeof(G1Ctrl) <= G1_CTRL_BYTES, "control block too large");
@@ -189,6 +202,16 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
       mbar_init(&ctl->tfull[b], 1);
       mbar_init(&ctl->tempty[b], 8);
     }
+#pragma unroll
+    for (int r = 0; r < G1_SC_RING; ++r) {
+      mbar_init(&ctl->sfull[r], 1);
+      mbar_init(&ctl->sempty[r], 8);
+    }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(&ctl->ufull[q], 1);
+      mbar_init(&ctl->uempty[q], 8);
+    }
     mbar_init(&ctl->mma_done, 1);
     ctl->abort_flag = 0;
     fence_mbar_init();
@@ -211,14 +234,48 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
-      // First unit (blockIdx.x < n_units): while the gather still runs, fill every stage with its
-      // weight tile, so HBM is busy before the first row tile exists. Then wait for the gather,
-      // let GEMM2 be scheduled, and complete the stages with their row tiles. (Pulling further
-      // weight tiles into L2 with bulk prefetches at this point was measured slower.)
+      // W13 block scales of unit number un (this CTA's count) into slot un & 1.
+      auto issue_unit_scales = [&](uint32_t un, int e, int j) -> bool {
+        const int q = un & 1;
+        if (!mbar_wait(&ctl->uempty[q], ((un >> 1) & 1u) ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) return false;
+        mbar_arrive_expect_tx(&ctl->ufull[q], 2 * HB * 4);
+        bulk_g2s(ctl->w_sc[q][0], p.w13_scale + (static_cast<size_t>(e) * G1B + j) * HB, HB * 4, &ctl->ufull[q]);
+        bulk_g2s(ctl->w_sc[q][1], p.w13_scale + (static_cast<size_t>(e) * G1B + G1_NT + j) * HB, HB * 4,
+                 &ctl->ufull[q]);
+        return true;
+      };
+      // Row scales of the tile's K blocks kb0 .. kb0 + G1_SC_KB - 1 into the slot of group g.
+      auto issue_scale_group = [&](uint32_t g, int tile, int kb0) -> bool {
+        const int r = g % G1_SC_RING;
+        if (!mbar_wait(&ctl->sempty[r], ((g / G1_SC_RING) & 1u) ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) return false;
+        mbar_arrive_expect_tx(&ctl->sfull[r], G1_SC_KB * TILE_M * 4);
+        bulk_g2s(ctl->a_sc[r], p.a_scale + (static_cast<size_t>(tile) * HB + kb0) * TILE_M, G1_SC_KB * TILE_M * 4,
+                 &ctl->sfull[r]);
+        return true;
+      };
+      // Stage of K block number it (tile's K block kb): the routed-row tile and the weight tile.
+      auto issue_block = [&](uint32_t it, const uint8_t* a_src, const uint8_t* b_src, int kb) -> bool {
+        const int s = it % G1_STAGES;
+        if (!mbar_wait(&ctl->empty[s], ((it / G1_STAGES) & 1u) ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) return false;
+        uint8_t* sa = smem + s * G1_STAGE_BYTES;
+        mbar_arrive_expect_tx(&ctl->full[s], G1_STAGE_BYTES);
+        bulk_g2s(sa, a_src + static_cast<size_t>(kb) * TILE_BYTES, G1_A_BYTES, &ctl->full[s]);
+        bulk_g2s_hint(sa + G1_A_BYTES, b_src + static_cast<size_t>(kb) * G1_B_BYTES, G1_B_BYTES, &ctl->full[s],
+                      pol_w);
+        return true;
+      };
+      // First unit (blockIdx.x < n_units): while the gather still runs, fetch the unit's W13
+      // scales and fill every stage with its weight tile, so HBM is busy before the first row
+      // tile exists. Then wait for the gather, let GEMM2 be scheduled, and complete the stages
+      // with their row tiles and row scales. (Pulling further weight tiles into L2 with bulk
+      // prefetches at this point was measured slower.)
+      uint32_t it = 0, units_issued = 0, groups_issued = 0;
       {
         const int tile = blockIdx.x / G1_NT, j = blockIdx.x % G1_NT;
         const int e = tile_expert(&ctl->map, p.E_local, tile);
         const uint8_t* b_src = p.w13p + (static_cast<size_t>(e) * G1_NT + j) * HB * G1_B_BYTES;
+        issue_unit_scales(0, e, j);   // slot 0 is free: the wait returns at once
+        units_issued = 1;
 #pragma unroll
         for (int s = 0; s < G1_STAGES; ++s) {
           mbar_arrive_expect_tx(&ctl->full[s], G1_STAGE_BYTES);
@@ -227,32 +284,46 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
         }
         wait_prerequisite_grids();
         allow_dependent_launch();
+        issue_scale_group(0, tile, 0);   // slot 0 is free: the wait returns at once
+        groups_issued = 1;
         const uint8_t* a_src = p.a_tiled + static_cast<size_t>(tile) * HB * TILE_BYTES;
 #pragma unroll
         for (int s = 0; s < G1_STAGES; ++s)
           bulk_g2s(smem + s * G1_STAGE_BYTES, a_src + static_cast<size_t>(s) * TILE_BYTES, G1_A_BYTES,
                    &ctl->full[s]);
+        it = G1_STAGES;
       }
-      uint32_t it = G1_STAGES;
+      static_assert(G1_STAGES <= G1_SC_KB, "the first stages lie in the first scale group");
       for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
         const int tile = u / G1_NT, j = u % G1_NT;
         const int e = tile_expert(&ctl->map, p.E_local, tile);
         const uint8_t* a_src = p.a_tiled + static_cast<size_t>(tile) * HB * TILE_BYTES;
         const uint8_t* b_src = p.w13p + (static_cast<size_t>(e) * G1_NT + j) * HB * G1_B_BYTES;
-        for (int kb = u == static_cast<int>(blockIdx.x) ? G1_STAGES : 0; kb < HB; ++kb, ++it) {
-          const int s = it % G1_STAGES;
-          const uint32_t ph = (it / G1_STAGES) & 1u;
-          if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) break;
-          uint8_t* sa = smem + s * G1_STAGE_BYTES;
-          mbar_arrive_expect_tx(&ctl->full[s], G1_STAGE_BYTES);
-          bulk_g2s(sa, a_src + static_cast<size_t>(kb) * TILE_BYTES, G1_A_BYTES, &ctl->full[s]);
-          bulk_g2s_hint(sa + G1_A_BYTES, b_src + static_cast<size_t>(kb) * G1_B_BYTES, G1_B_BYTES,
-                        &ctl->full[s], pol_w);
+        const bool first = u == static_cast<int>(blockIdx.x);
+        if (!first) {
+          if (!issue_unit_scales(units_issued, e, j)) break;
+          ++units_issued;
         }
+        bool ok = true;
+        for (int kb = first ? G1_STAGES : 0; kb < HB; ++kb, ++it) {
+          if (kb % G1_SC_KB == 0) {
+            if (!issue_scale_group(groups_issued, tile, kb)) {
+              ok = false;
+              break;
+            }
+            ++groups_issued;
+          }
+          if (!issue_block(it, a_src, b_src, kb)) {
+            ok = false;
+            break;
+          }
+        }
+        if (!ok) break;
       }
       const uint32_t issued = it;
       if (!*abort_flag) {
         // Drain: wait until the MMAs have released every stage, so no async arrive is pending.
+        // (Every scale copy is waited for by the epilogue.)
         for (uint32_t jt = issued; jt < issued + G1_STAGES; ++jt) {
           if (!mbar_wait(&ctl->empty[jt % G1_STAGES], ((jt / G1_STAGES) & 1u) ^ 1u, abort_flag,
                          ST_TIMEOUT_PRODUCER))
@@ -264,6 +335,14 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
         for (uint32_t i = 1; i <= G1_STAGES && i <= issued; ++i) {
           const uint32_t jt = issued - i;
           mbar_wait_drain(&ctl->full[jt % G1_STAGES], (jt / G1_STAGES) & 1u);
+        }
+        for (uint32_t i = 1; i <= G1_SC_RING && i <= groups_issued; ++i) {
+          const uint32_t g = groups_issued - i;
+          mbar_wait_drain(&ctl->sfull[g % G1_SC_RING], (g / G1_SC_RING) & 1u);
+        }
+        for (uint32_t i = 1; i <= 2 && i <= units_issued; ++i) {
+          const uint32_t un = units_issued - i;
+          mbar_wait_drain(&ctl->ufull[un & 1], (un >> 1) & 1u);
         }
       }
     }
@@ -315,33 +394,46 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
     const int hf = (warp - 4) >> 2;     // column half: 64 X1 + 64 X2 columns
     const int row = q4 * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(q4 * 32) << 16;
-    uint32_t it = 0, unit_no = 0;
+    uint32_t it = 0, unit_no = 0, grp = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++unit_no) {
       const int tile = u / G1_NT, j = u % G1_NT;
-      const int e = tile_expert(&ctl->map, p.E_local, tile);
-      const float* sa_ptr = p.a_scale + static_cast<size_t>(tile) * HB * TILE_M + row;
-      const float* sg_ptr = p.w13_scale + (static_cast<size_t>(e) * G1B + j) * HB;
-      const float* su_ptr = p.w13_scale + (static_cast<size_t>(e) * G1B + G1_NT + j) * HB;
       float accg[64], accu[64];
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
         accg[i] = 0.0f;
         accu[i] = 0.0f;
       }
-      // Scale factors of the next K block are loaded one block ahead, off the critical path.
-      float na = __ldg(sa_ptr), ng = __ldg(sg_ptr), nu = __ldg(su_ptr);
-      bool aborted = false;
-      for (int kb = 0; kb < HB; ++kb, ++it) {
-        const float fg = na * ng, fu = na * nu;
-        if (kb + 1 < HB) {
-          na = __ldg(sa_ptr + (kb + 1) * TILE_M);
-          ng = __ldg(sg_ptr + kb + 1);
-          nu = __ldg(su_ptr + kb + 1);
+      // The unit's W13 scales and each K block's row scales come through shared memory (copied by
+      // the producer); each slot is released once this warp has read it.
+      const int uq = unit_no & 1;
+      bool aborted = !mbar_wait_warp(&ctl->ufull[uq], (unit_no >> 1) & 1u, abort_flag, ST_TIMEOUT_EPILOGUE);
+      if (!aborted) mbar_observe(&ctl->ufull[uq], (unit_no >> 1) & 1u);
+      const float* wg = ctl->w_sc[uq][0];
+      const float* wu = ctl->w_sc[uq][1];
+      for (int kb = 0; kb < HB && !aborted; ++kb, ++it) {
+        const int r = grp % G1_SC_RING;
+        if (kb % G1_SC_KB == 0) {
+          if (!mbar_wait_warp(&ctl->sfull[r], (grp / G1_SC_RING) & 1u, abort_flag, ST_TIMEOUT_EPILOGUE)) {
+            aborted = true;
+            break;
+          }
+          mbar_observe(&ctl->sfull[r], (grp / G1_SC_RING) & 1u);
+        }
+        const float na = ctl->a_sc[r][kb % G1_SC_KB][row];
+        const float fg = na * wg[kb], fu = na * wu[kb];
+        if (kb % G1_SC_KB == G1_SC_KB - 1) {
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&ctl->sempty[r]);
+          ++grp;
         }
         if (!promote_block(ctl, tmem, t_lane, hf, it, fg, accg, fu, accu, abort_flag)) {
           aborted = true;
           break;
         }
+      }
+      if (!aborted) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->uempty[uq]);
       }
       // Every epilogue thread passes this barrier once per unit; the OR makes the decision
       // to stop uniform, so no thread is left waiting on a barrier the others skipped.

@@ -63,7 +63,7 @@ constexpr int G2_A_BYTES = TILE_BYTES;      // one of hi / lo
 constexpr int G2_B_BYTES = 2 * TILE_BYTES;  // 256 W2 rows x 128 K bytes
 constexpr int G2_STAGE_BYTES = 2 * G2_A_BYTES + G2_B_BYTES;
 constexpr int G2_THREADS = GEMM_THREADS;
-constexpr int G2_CTRL_BYTES = 4096;
+constexpr int G2_CTRL_BYTES = 20480;
 constexpr int G2_SMEM = G2_STAGES * G2_STAGE_BYTES + G2_CTRL_BYTES + 1024;
 
 // Units are claimed at run time from a global counter (tile-major order), so CTAs that start
@@ -79,9 +79,16 @@ struct G2Ctrl {
   int unit[G2_UNIT_RING];
   uint64_t tfull[ACC_BUFS];
   uint64_t tempty[ACC_BUFS];
+  uint64_t sfull[2];             // block scales of the unit with this parity landed
+  uint64_t sempty[2];            // ... and read by the eight epilogue warps
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort_flag;
+  // Block scales of a unit, copied by the producer (loading them from global memory in the
+  // epilogue stalled it on every K block): C's c_scale[tile, 0..15, 0..127] and W2's
+  // w2_scale[e, 2 nt .. 2 nt + 1, 0..15], two slots by unit parity.
+  alignas(16) float c_sc[2][IB][TILE_M];
+  alignas(16) float w_sc[2][2][IB];
   TileMap map;
 };
 static_assert(sizeof(G2Ctrl) <= G2_CTRL_BYTES, "control block too large");
@@ -128,6 +135,11 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
       mbar_init(&ctl->ufull[r], 1);
       mbar_init(&ctl->uempty[r], 9);   // the MMA warp and the eight epilogue warps
     }
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      mbar_init(&ctl->sfull[q], 1);
+      mbar_init(&ctl->sempty[q], 8);
+    }
     mbar_init(&ctl->mma_done, 1);
     ctl->abort_flag = 0;
     fence_mbar_init();
@@ -149,7 +161,7 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
     // ---------------- producer ----------------
     if (lane == 0) {
       const uint64_t pol_w = policy_evict_first();
-      uint32_t it = 0;
+      uint32_t it = 0, units_issued = 0;
       int ready_tile = -1;
       for (uint32_t k = 0; !*abort_flag; ++k) {
         // Claim the next unit and hand it to the MMA and epilogue warps.
@@ -169,6 +181,14 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
         if (tile != ready_tile) {
           if (!wait_tile_ready(p.tile_ready + tile, abort_flag)) break;
           ready_tile = tile;
+        }
+        {
+          const int q = units_issued & 1;
+          if (!mbar_wait(&ctl->sempty[q], ((units_issued >> 1) & 1u) ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) break;
+          mbar_arrive_expect_tx(&ctl->sfull[q], (IB * TILE_M + 2 * IB) * 4);
+          bulk_g2s(ctl->c_sc[q], p.c_scale + static_cast<size_t>(tile) * IB * TILE_M, IB * TILE_M * 4, &ctl->sfull[q]);
+          bulk_g2s(ctl->w_sc[q], p.w2_scale + (static_cast<size_t>(e) * HB + 2 * nt) * IB, 2 * IB * 4, &ctl->sfull[q]);
+          ++units_issued;
         }
         for (int ib = 0; ib < IB; ++ib, ++it) {
           const int s = it % G2_STAGES;
@@ -196,6 +216,10 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
         for (uint32_t i = 1; i <= G2_STAGES && i <= issued; ++i) {
           const uint32_t jt = issued - i;
           mbar_wait_drain(&ctl->full[jt % G2_STAGES], (jt / G2_STAGES) & 1u);
+        }
+        for (uint32_t i = 1; i <= 2 && i <= units_issued; ++i) {
+          const uint32_t un = units_issued - i;
+          mbar_wait_drain(&ctl->sfull[un & 1], (un >> 1) & 1u);
         }
       }
     }
@@ -258,33 +282,35 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
       const int tile = u / G2_NT, nt = u % G2_NT;
       const TileInfo ti = locate(&ctl->map, p.counts, p.E_local, tile, p.slots);
       const int e = ti.e;
-      const float* cs_ptr = p.c_scale + static_cast<size_t>(tile) * IB * TILE_M + row;
-      const float* ws0 = p.w2_scale + (static_cast<size_t>(e) * HB + 2 * nt) * IB;
-      const float* ws1 = ws0 + IB;
+      const int slot = ti.m * TILE_M + row;
+      // The route weight is first needed after the K loop; its load is issued now.
+      const float w = row < ti.rows ? __ldg(p.route_w + static_cast<size_t>(e) * p.slots + slot) : 0.0f;
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
-      // c_scale is written by GEMM1, which may still be running: acquire the tile's counter
-      // first (it is complete by now unless this CTA is far ahead), then read through L2.
-      bool aborted = !wait_tile_ready(p.tile_ready + tile, abort_flag);
-      float nc = aborted ? 0.0f : __ldcg(cs_ptr), n0 = __ldg(ws0), n1 = __ldg(ws1);
+      // The unit's scales come through shared memory: the producer copies them once the tile's
+      // readiness counter shows GEMM1 has stored C and c_scale.
+      const int uq = k & 1;
+      bool aborted = !mbar_wait_warp(&ctl->sfull[uq], (k >> 1) & 1u, abort_flag, ST_TIMEOUT_EPILOGUE);
+      if (!aborted) mbar_observe(&ctl->sfull[uq], (k >> 1) & 1u);
+      const float* cs = &ctl->c_sc[uq][0][row];
+      const float* ws0 = ctl->w_sc[uq][0];
+      const float* ws1 = ctl->w_sc[uq][1];
       for (int ib = 0; ib < IB && !aborted; ++ib, ++it) {
-        const float f0 = nc * n0, f1 = nc * n1;
-        if (ib + 1 < IB) {
-          nc = __ldcg(cs_ptr + (ib + 1) * TILE_M);
-          n0 = __ldg(ws0 + ib + 1);
-          n1 = __ldg(ws1 + ib + 1);
-        }
+        const float nc = cs[ib * TILE_M];
+        const float f0 = nc * ws0[ib], f1 = nc * ws1[ib];
         if (!promote_block(ctl, tmem, t_lane, hf, it, f0, acc, f1, acc + 64, abort_flag)) {
           aborted = true;
           break;
         }
       }
+      if (!aborted) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&ctl->sempty[uq]);
+      }
       if (named_bar_or(1, 256, aborted)) break;
 
       if (row < ti.rows) {
-        const int slot = ti.m * TILE_M + row;
-        const float w = p.route_w[static_cast<size_t>(e) * p.slots + slot];
         const size_t d = static_cast<size_t>(ctl->map.dense_off[e] + slot);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {

@@ -187,6 +187,11 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
   return true;
 }
 
+// After a warp-wide wait has seen a phase complete: every lane observes the completion itself
+// (an acquire of its own) before it reads data that the async proxy wrote under that barrier.
+// The phase cannot advance meanwhile, because the slot is released only after these reads.
+__device__ __forceinline__ void mbar_observe(uint64_t* bar, uint32_t parity) { (void)mbar_try_wait(bar, parity); }
+
 // Warp-uniform bounded wait: lane 0 waits, the result is broadcast to the warp.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
                                                volatile int* abort_flag, int who) {
