@@ -173,7 +173,10 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
         mbar_arrive(&ctl->ufull[r]);
         if (u < 0) break;
         const int tile = u / G2_NT, nt = u % G2_NT;
-        const int e = tile_expert(&ctl->map, p.E_local, tile);
+        const TileInfo ti = locate(&ctl->map, p.counts, p.E_local, tile, p.slots);
+        const int e = ti.e;
+        // A tile of at most 64 routes runs M = 64 MMAs: only its first 64 rows of C are read.
+        const uint32_t c_bytes = ti.rows <= TILE_M / 2 ? G2_A_BYTES / 2 : G2_A_BYTES;
         const size_t a_off = static_cast<size_t>(tile) * IB * TILE_BYTES;
         const uint8_t* b_src = p.w2p + (static_cast<size_t>(e) * G2_NT + nt) * IB * G2_B_BYTES;
         // This grid may start while GEMM1 still runs (programmatic launch): the tile's C must be
@@ -195,11 +198,9 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
           const uint32_t ph = (it / G2_STAGES) & 1u;
           if (!mbar_wait(&ctl->empty[s], ph ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) break;
           uint8_t* st = smem + s * G2_STAGE_BYTES;
-          mbar_arrive_expect_tx(&ctl->full[s], G2_STAGE_BYTES);
-          bulk_g2s(st, p.c_hi + a_off + static_cast<size_t>(ib) * TILE_BYTES, G2_A_BYTES,
-                   &ctl->full[s]);
-          bulk_g2s(st + G2_A_BYTES, p.c_lo + a_off + static_cast<size_t>(ib) * TILE_BYTES,
-                   G2_A_BYTES, &ctl->full[s]);
+          mbar_arrive_expect_tx(&ctl->full[s], 2 * c_bytes + G2_B_BYTES);
+          bulk_g2s(st, p.c_hi + a_off + static_cast<size_t>(ib) * TILE_BYTES, c_bytes, &ctl->full[s]);
+          bulk_g2s(st + G2_A_BYTES, p.c_lo + a_off + static_cast<size_t>(ib) * TILE_BYTES, c_bytes, &ctl->full[s]);
           bulk_g2s_hint(st + 2 * G2_A_BYTES, b_src + static_cast<size_t>(ib) * G2_B_BYTES,
                         G2_B_BYTES, &ctl->full[s], pol_w);
         }
@@ -226,12 +227,15 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(128, ACC_COLS);
       uint32_t it = 0;
       bool stop = false;
       for (uint32_t k = 0; !stop; ++k) {
         const int u = g2_next_unit(ctl, k, abort_flag, false);
         if (u < 0) break;
+        // M = 64 for a tile of at most 64 routes: the accumulator then holds row 16 j + i in TMEM
+        // lane 32 j + i (i < 16), half the tensor work of M = 128.
+        const TileInfo ti = locate(&ctl->map, p.counts, p.E_local, u / G2_NT, p.slots);
+        const uint32_t idesc = idesc_e4m3_f32(ti.rows <= TILE_M / 2 ? 64 : 128, ACC_COLS);
         for (int ib = 0; ib < IB && !stop; ++ib, ++it) {
           const int s = it % G2_STAGES;
           const uint32_t ph = (it / G2_STAGES) & 1u;
@@ -273,7 +277,6 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
     regs_inc<REGS_EPI>();
     const int q4 = warp & 3;
     const int hf = (warp - 4) >> 2;    // which 64 columns of each 128-wide half
-    const int row = q4 * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(q4 * 32) << 16;
     uint32_t it = 0;
     for (uint32_t k = 0;; ++k) {
@@ -282,6 +285,10 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
       const int tile = u / G2_NT, nt = u % G2_NT;
       const TileInfo ti = locate(&ctl->map, p.counts, p.E_local, tile, p.slots);
       const int e = ti.e;
+      // Row of the tile this thread's TMEM lane holds: lane q4 * 32 + lane for M = 128; for the
+      // M = 64 MMAs of a tile of at most 64 routes, row 16 q4 + lane in lanes 0-15 of each
+      // quarter, and no row (TILE_M) in lanes 16-31.
+      const int row = ti.rows <= TILE_M / 2 ? (lane < 16 ? q4 * 16 + lane : TILE_M) : q4 * 32 + lane;
       const int slot = ti.m * TILE_M + row;
       // The route weight is first needed after the K loop; its load is issued now.
       const float w = row < ti.rows ? __ldg(p.route_w + static_cast<size_t>(e) * p.slots + slot) : 0.0f;
@@ -293,7 +300,7 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
       const int uq = k & 1;
       bool aborted = !mbar_wait_warp(&ctl->sfull[uq], (k >> 1) & 1u, abort_flag, ST_TIMEOUT_EPILOGUE);
       if (!aborted) mbar_observe(&ctl->sfull[uq], (k >> 1) & 1u);
-      const float* cs = &ctl->c_sc[uq][0][row];
+      const float* cs = &ctl->c_sc[uq][0][row < TILE_M ? row : 0];
       const float* ws0 = ctl->w_sc[uq][0];
       const float* ws1 = ctl->w_sc[uq][1];
       for (int ib = 0; ib < IB && !aborted; ++ib, ++it) {
