@@ -254,12 +254,14 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
         return true;
       };
       // Stage of K block number it (tile's K block kb): the routed-row tile and the weight tile.
-      auto issue_block = [&](uint32_t it, const uint8_t* a_src, const uint8_t* b_src, int kb) -> bool {
+      // A tile of at most 64 routes runs M = 64 MMAs and needs only its first 64 rows (a_bytes).
+      auto issue_block = [&](uint32_t it, const uint8_t* a_src, uint32_t a_bytes, const uint8_t* b_src,
+                             int kb) -> bool {
         const int s = it % G1_STAGES;
         if (!mbar_wait(&ctl->empty[s], ((it / G1_STAGES) & 1u) ^ 1u, abort_flag, ST_TIMEOUT_PRODUCER)) return false;
         uint8_t* sa = smem + s * G1_STAGE_BYTES;
-        mbar_arrive_expect_tx(&ctl->full[s], G1_STAGE_BYTES);
-        bulk_g2s(sa, a_src + static_cast<size_t>(kb) * TILE_BYTES, G1_A_BYTES, &ctl->full[s]);
+        mbar_arrive_expect_tx(&ctl->full[s], a_bytes + G1_B_BYTES);
+        bulk_g2s(sa, a_src + static_cast<size_t>(kb) * TILE_BYTES, a_bytes, &ctl->full[s]);
         bulk_g2s_hint(sa + G1_A_BYTES, b_src + static_cast<size_t>(kb) * G1_B_BYTES, G1_B_BYTES, &ctl->full[s],
                       pol_w);
         return true;
@@ -272,13 +274,15 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
       uint32_t it = 0, units_issued = 0, groups_issued = 0;
       {
         const int tile = blockIdx.x / G1_NT, j = blockIdx.x % G1_NT;
-        const int e = tile_expert(&ctl->map, p.E_local, tile);
+        const TileInfo ti = locate(&ctl->map, p.counts, p.E_local, tile, p.slots);
+        const int e = ti.e;
+        const uint32_t a_bytes = ti.rows <= TILE_M / 2 ? G1_A_BYTES / 2 : G1_A_BYTES;
         const uint8_t* b_src = p.w13p + (static_cast<size_t>(e) * G1_NT + j) * HB * G1_B_BYTES;
         issue_unit_scales(0, e, j);   // slot 0 is free: the wait returns at once
         units_issued = 1;
 #pragma unroll
         for (int s = 0; s < G1_STAGES; ++s) {
-          mbar_arrive_expect_tx(&ctl->full[s], G1_STAGE_BYTES);
+          mbar_arrive_expect_tx(&ctl->full[s], a_bytes + G1_B_BYTES);
           bulk_g2s_hint(smem + s * G1_STAGE_BYTES + G1_A_BYTES, b_src + static_cast<size_t>(s) * G1_B_BYTES,
                         G1_B_BYTES, &ctl->full[s], pol_w);
         }
@@ -289,14 +293,16 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
         const uint8_t* a_src = p.a_tiled + static_cast<size_t>(tile) * HB * TILE_BYTES;
 #pragma unroll
         for (int s = 0; s < G1_STAGES; ++s)
-          bulk_g2s(smem + s * G1_STAGE_BYTES, a_src + static_cast<size_t>(s) * TILE_BYTES, G1_A_BYTES,
+          bulk_g2s(smem + s * G1_STAGE_BYTES, a_src + static_cast<size_t>(s) * TILE_BYTES, a_bytes,
                    &ctl->full[s]);
         it = G1_STAGES;
       }
       static_assert(G1_STAGES <= G1_SC_KB, "the first stages lie in the first scale group");
       for (int u = blockIdx.x; u < n_units && !*abort_flag; u += gridDim.x) {
         const int tile = u / G1_NT, j = u % G1_NT;
-        const int e = tile_expert(&ctl->map, p.E_local, tile);
+        const TileInfo ti = locate(&ctl->map, p.counts, p.E_local, tile, p.slots);
+        const int e = ti.e;
+        const uint32_t a_bytes = ti.rows <= TILE_M / 2 ? G1_A_BYTES / 2 : G1_A_BYTES;
         const uint8_t* a_src = p.a_tiled + static_cast<size_t>(tile) * HB * TILE_BYTES;
         const uint8_t* b_src = p.w13p + (static_cast<size_t>(e) * G1_NT + j) * HB * G1_B_BYTES;
         const bool first = u == static_cast<int>(blockIdx.x);
@@ -313,7 +319,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
             }
             ++groups_issued;
           }
-          if (!issue_block(it, a_src, b_src, kb)) {
+          if (!issue_block(it, a_src, a_bytes, b_src, kb)) {
             ok = false;
             break;
           }
@@ -349,10 +355,13 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
   } else if (warp == 1) {
     // ---------------- MMA issuer ----------------
     if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(128, ACC_COLS);
       uint32_t it = 0;
       bool stop = false;
       for (int u = blockIdx.x; u < n_units && !stop; u += gridDim.x) {
+        // M = 64 for a tile of at most 64 routes: row 16 j + i of the accumulator is TMEM lane
+        // 32 j + i (i < 16), half the tensor work of M = 128.
+        const TileInfo ti = locate(&ctl->map, p.counts, p.E_local, u / G1_NT, p.slots);
+        const uint32_t idesc = idesc_e4m3_f32(ti.rows <= TILE_M / 2 ? 64 : 128, ACC_COLS);
         for (int kb = 0; kb < HB && !stop; ++kb, ++it) {
           const int s = it % G1_STAGES;
           const uint32_t ph = (it / G1_STAGES) & 1u;
@@ -392,11 +401,17 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
     regs_inc<REGS_EPI>();
     const int q4 = warp & 3;            // TMEM lane quadrant this warp may access
     const int hf = (warp - 4) >> 2;     // column half: 64 X1 + 64 X2 columns
-    const int row = q4 * 32 + lane;
     const uint32_t t_lane = static_cast<uint32_t>(q4 * 32) << 16;
     uint32_t it = 0, unit_no = 0, grp = 0;
     for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++unit_no) {
       const int tile = u / G1_NT, j = u % G1_NT;
+      // Row of the tile this thread's TMEM lane holds: lane q4 * 32 + lane for M = 128; for the
+      // M = 64 MMAs of a tile of at most 64 routes, row 16 q4 + lane in lanes 0-15 of each quarter
+      // and none in lanes 16-31 (they compute on what their lanes hold and store nothing). The
+      // rows past 64 of such a tile's C are never read: GEMM2 reads 64 rows of it.
+      const bool small = locate(&ctl->map, p.counts, p.E_local, tile, p.slots).rows <= TILE_M / 2;
+      const bool has_row = !small || lane < 16;
+      const int row = small ? q4 * 16 + (lane & 15) : q4 * 32 + lane;
       float accg[64], accu[64];
 #pragma unroll
       for (int i = 0; i < 64; ++i) {
@@ -451,7 +466,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
         accg[i] = c;
         amax = fmaxf(amax, fabsf(c));
       }
-      ctl->amax[unit_no & 1][hf][row] = amax;
+      if (has_row) ctl->amax[unit_no & 1][hf][row] = amax;
       named_bar_or(2, 256, false);
       amax = fmaxf(amax, ctl->amax[unit_no & 1][hf ^ 1][row]);
       const float scale = amax > 0.0f ? amax / 448.0f : 1.0f;
@@ -466,10 +481,12 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
         quant_hi_lo16(&accg[ch * 16], hi, lo);
         const int c16 = hf * 4 + ch;
         const size_t off = blk + ((c16 ^ (row & 7)) << 4);
-        *reinterpret_cast<uint4*>(p.c_hi + off) = hi;
-        *reinterpret_cast<uint4*>(p.c_lo + off) = lo;
+        if (has_row) {
+          *reinterpret_cast<uint4*>(p.c_hi + off) = hi;
+          *reinterpret_cast<uint4*>(p.c_lo + off) = lo;
+        }
       }
-      if (hf == 0) p.c_scale[(static_cast<size_t>(tile) * IB + j) * TILE_M + row] = scale;
+      if (hf == 0 && has_row) p.c_scale[(static_cast<size_t>(tile) * IB + j) * TILE_M + row] = scale;
       // Publish: once every epilogue thread's C stores of this unit are visible GPU-wide, count
       // the column block as done for the tile (GEMM2 starts a tile at G1_NT).
       __threadfence();
