@@ -127,7 +127,7 @@ __device__ __forceinline__ void tmem_ld64(uint32_t taddr, float (&v)[64]) {
 // promoted into acc0 with factor f0, the same columns of the second half into acc1 with f1.
 // An accumulator is released as soon as its values are in registers, before the FMAs, so the
 // tensor core can refill it while the promotion runs.
-template <class Ctrl>
+template <class Ctrl, bool kSpin = false>
 __device__ __forceinline__ bool promote_block(Ctrl* ctl, uint32_t tmem, uint32_t t_lane, int hf,
                                               uint32_t it, float f0, float* acc0, float f1,
                                               float* acc1, volatile int* abort_flag) {
@@ -137,7 +137,7 @@ __device__ __forceinline__ bool promote_block(Ctrl* ctl, uint32_t tmem, uint32_t
     const uint32_t hidx = ACC_SPLIT == 2 ? 2 * it + half : it;
     const uint32_t q = hidx % ACC_BUFS, use = hidx / ACC_BUFS;
     if (ACC_SPLIT == 2 || half == 0) {
-      if (!mbar_wait_warp(&ctl->tfull[q], use & 1u, abort_flag, ST_TIMEOUT_EPILOGUE)) return false;
+      if (!mbar_wait_warp(&ctl->tfull[q], use & 1u, abort_flag, ST_TIMEOUT_EPILOGUE, kSpin)) return false;
       tc_fence_after();
     }
     const uint32_t col = q * ACC_COLS + (ACC_SPLIT == 1 ? half * 128u : 0u) + hf * 64u;

@@ -239,7 +239,7 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
         for (int ib = 0; ib < IB && !stop; ++ib, ++it) {
           const int s = it % G2_STAGES;
           const uint32_t ph = (it / G2_STAGES) & 1u;
-          if (!mbar_wait(&ctl->full[s], ph, abort_flag, ST_TIMEOUT_MMA)) {
+          if (!mbar_wait_spin(&ctl->full[s], ph, abort_flag, ST_TIMEOUT_MMA)) {
             stop = true;
             break;
           }
@@ -249,7 +249,7 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
           for (int h = 0; h < ACC_SPLIT; ++h) {   // output columns [ACC_COLS h, ACC_COLS (h+1))
             const uint32_t hidx = ACC_SPLIT * it + h;
             const uint32_t q = hidx % ACC_BUFS, use = hidx / ACC_BUFS;
-            if (!mbar_wait(&ctl->tempty[q], (use & 1u) ^ 1u, abort_flag, ST_TIMEOUT_MMA)) {
+            if (!mbar_wait_spin(&ctl->tempty[q], (use & 1u) ^ 1u, abort_flag, ST_TIMEOUT_MMA)) {
               stop = true;
               break;
             }
@@ -306,7 +306,7 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
       for (int ib = 0; ib < IB && !aborted; ++ib, ++it) {
         const float nc = cs[ib * TILE_M];
         const float f0 = nc * ws0[ib], f1 = nc * ws1[ib];
-        if (!promote_block(ctl, tmem, t_lane, hf, it, f0, acc, f1, acc + 64, abort_flag)) {
+        if (!promote_block<G2Ctrl, true>(ctl, tmem, t_lane, hf, it, f0, acc, f1, acc + 64, abort_flag)) {
           aborted = true;
           break;
         }

@@ -192,11 +192,44 @@ __device__ __forceinline__ bool mbar_wait_drain(uint64_t* bar, uint32_t parity) 
 // The phase cannot advance meanwhile, because the slot is released only after these reads.
 __device__ __forceinline__ void mbar_observe(uint64_t* bar, uint32_t parity) { (void)mbar_try_wait(bar, parity); }
 
+// Non-suspending poll of an mbarrier phase.
+__device__ __forceinline__ bool mbar_test_wait(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait by polling, for the hand-offs on a GEMM's critical path (stage -> MMA -> epilogue ->
+// MMA): a suspended try_wait wakes measurably later after the phase completes. The abort flag and
+// the clock are checked every 64 polls. Same limits and error reporting as mbar_wait.
+__device__ __forceinline__ bool mbar_wait_spin(uint64_t* bar, uint32_t parity, volatile int* abort_flag, int who) {
+  if (mbar_test_wait(bar, parity)) return true;
+  const unsigned long long t0 = globaltimer(), limit = wait_limit_ns();
+  for (uint32_t n = 1;; ++n) {
+    if (mbar_test_wait(bar, parity)) return true;
+    if ((n & 63u) == 0) {
+      if (*abort_flag) return false;
+      if (globaltimer() - t0 > limit) {
+        *abort_flag = 1;
+        report_status(who);
+        return false;
+      }
+    }
+  }
+}
+
 // Warp-uniform bounded wait: lane 0 waits, the result is broadcast to the warp.
 __device__ __forceinline__ bool mbar_wait_warp(uint64_t* bar, uint32_t parity,
-                                               volatile int* abort_flag, int who) {
+                                               volatile int* abort_flag, int who, bool spin = false) {
   int ok = 1;
-  if ((threadIdx.x & 31) == 0) ok = mbar_wait(bar, parity, abort_flag, who) ? 1 : 0;
+  if ((threadIdx.x & 31) == 0)
+    ok = (spin ? mbar_wait_spin(bar, parity, abort_flag, who) : mbar_wait(bar, parity, abort_flag, who)) ? 1 : 0;
   ok = __shfl_sync(0xffffffffu, ok, 0);
   __syncwarp();
   return ok != 0;
