@@ -441,7 +441,7 @@ __global__ void __launch_bounds__(G1_THREADS, 1) gemm1_swiglu_kernel(const __gri
           if (lane == 0) mbar_arrive(&ctl->sempty[r]);
           ++grp;
         }
-        if (!promote_block(ctl, tmem, t_lane, hf, it, fg, accg, fu, accu, abort_flag)) {
+        if (!promote_block<G1Ctrl, true>(ctl, tmem, t_lane, hf, it, fg, accg, fu, accu, abort_flag)) {
           aborted = true;
           break;
         }
