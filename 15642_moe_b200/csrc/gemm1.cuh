@@ -8,8 +8,11 @@
  *
  * One persistent CTA per SM, warp-specialised (three warpgroups, 384 threads):
  *   warp 0      producer: cp.async.bulk of the 16 KB A tile image (routed rows, written by the
- *               gather kernel) and the pre-swizzled 32 KB W13 tile into a 4-stage ring
- *   warp 1      MMA: per 128-K block, 4 x tcgen05.mma kind::f8f6f4 (M=128, K=32) over the
+ *               gather kernel; 8 KB for a tile of at most 64 routes) and the pre-swizzled 32 KB
+ *               W13 tile into a 4-stage ring, plus the block scales into shared memory (row
+ *               scales eight K blocks at a time, W13 scales once per unit)
+ *   warp 1      MMA: per 128-K block, 4 x tcgen05.mma kind::f8f6f4 (M=128, or 64 for a tile of
+ *               at most 64 routes; K=32) over the
  *               256 columns, as ACC_SPLIT groups of N = 256 / ACC_SPLIT, each group into its
  *               own TMEM accumulator; all 512 TMEM columns rotate as accumulators so K blocks
  *               stay in flight while the epilogue promotes earlier ones.

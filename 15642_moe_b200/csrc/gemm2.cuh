@@ -9,9 +9,12 @@
  *
  * Work unit = (128-row tile, 256 hidden rows of W2 = two 128-wide output halves). Same warp
  * roles and rotating TMEM accumulators as GEMM1:
- *   warp 0      producer (bulk copies: 16 KB hi + 16 KB lo + 32 KB W2 per stage, 3 stages)
- *   warp 1      MMA: per 128-K block, hi then lo for each of the 4 K steps (M=128, K=32), in
- *               ACC_SPLIT groups of N = 256 / ACC_SPLIT columns, each into its own accumulator
+ *   warp 0      producer (bulk copies: 16 KB hi + 16 KB lo + 32 KB W2 per stage, 3 stages; 8 KB
+ *               each of hi and lo for a tile of at most 64 routes), and per unit its block scales
+ *               (c_scale of the tile, two rows of w2_scale) into shared memory
+ *   warp 1      MMA: per 128-K block, hi then lo for each of the 4 K steps (M = 128, or 64 for a
+ *               tile of at most 64 routes; K = 32), in ACC_SPLIT groups of N = 256 / ACC_SPLIT
+ *               columns, each into its own accumulator
  *   warps 4-11  epilogue: per accumulator, promote with c_scale[row, kb] * w2_scale[hb, kb];
  *               at the end multiply by the route weight and write the fp32 rows to `partial`
  *               (dense: one row per local route).
