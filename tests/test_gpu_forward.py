@@ -198,3 +198,30 @@ def test_forward_two_tile_experts(pkg, oracle):
     ref = oracle.moe_forward(**oracle.to_numpy_inputs(inp))
     r = oracle.check_tolerance(ref, out_bits(out), ATOL, RTOL)
     assert r["bad"] == 0, r
+
+
+def test_forward_tile_size_boundaries(pkg, oracle):
+    """Local expert counts chosen at the kernels' tile-shape boundaries: 64 routes (one tile run with
+    M = 64 MMAs), 65 (one M = 128 tile), 128 (one full tile), 129 (a full tile plus a one-route M = 64
+    tile) and 1. The logits make each token's eight picks explicit: +10 on the chosen experts (group 0
+    holds the local ones, groups 1-3 the rest of the eight), -10 elsewhere, zero bias."""
+    T = 129
+    cfg = pkg.MoEConfig(T=T, seed=11)
+    inp = pkg.make_inputs(cfg, "cuda")
+    logits = torch.full((T, 256), -10.0)
+    want = {0: 64, 1: 65, 2: 128, 3: 129, 4: 1}
+    for t in range(T):
+        local = [e for e, n in want.items() if t < n]
+        others = [32 * (1 + g) + t % 4 * 3 + i for g in range(3) for i in range(3)][:8 - len(local)]
+        for e in local + others:
+            logits[t, e] = 10.0
+    inp["routing_logits"] = logits.to(inp["routing_logits"].dtype).to("cuda")
+    inp["routing_bias"] = torch.zeros_like(inp["routing_bias"])
+    out, ws = forward_with_workspace(pkg, inp)
+    counts = region(ws, pkg.workspace_layout(T, 32), "counts", torch.int32, 32)
+    assert [int(counts[e]) for e in range(5)] == [64, 65, 128, 129, 1]
+    assert int(counts[5:].sum()) == 0
+    ref = oracle.moe_forward(**oracle.to_numpy_inputs(inp))
+    r = oracle.check_tolerance(ref, out_bits(out), ATOL, RTOL)
+    print(r)
+    assert r["bad"] == 0, r
