@@ -40,6 +40,14 @@ struct Gemm2Args {
   int* dense_base;          // [E_local + 1] written by CTA 0 for the combine
   const int* tile_ready;    // [tiles] GEMM1 column blocks done per tile; a tile is read at G1_NT
   int* unit_queue;          // zero at launch: the next unit to claim (dynamic schedule)
+  // When `direct` is set, a route that is its token's only local route is written straight into
+  // the token's output row (bf16, or fp32 when out_f32) instead of `partial`; the combine then
+  // skips that token. Its value is the combine's for a one-route token: round(0 + x).
+  void* out;
+  int out_f32;
+  const int* route_token;   // [E_local, slots] token of each expert slot
+  const int* token_nr;      // [slots] local routes of each token
+  int direct;
 };
 
 // Bounded wait until GEMM1 has stored all G1_NT column blocks of C for `tile` (acquire), then
@@ -293,8 +301,12 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
       // quarter, and no row (TILE_M) in lanes 16-31.
       const int row = ti.rows <= TILE_M / 2 ? (lane < 16 ? q4 * 16 + lane : TILE_M) : q4 * 32 + lane;
       const int slot = ti.m * TILE_M + row;
-      // The route weight is first needed after the K loop; its load is issued now.
+      // The route weight is first needed after the K loop; its load is issued now, and so is the
+      // route's token, whose local route count is loaded after the first K block (off the unit
+      // start): tok >= 0 marks a token's only local route.
       const float w = row < ti.rows ? __ldg(p.route_w + static_cast<size_t>(e) * p.slots + slot) : 0.0f;
+      const int tk = p.direct && row < ti.rows ? __ldg(p.route_token + static_cast<size_t>(e) * p.slots + slot) : -1;
+      int tk_nr = 0;
       float acc[128];
 #pragma unroll
       for (int i = 0; i < 128; ++i) acc[i] = 0.0f;
@@ -313,14 +325,39 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
           aborted = true;
           break;
         }
+        if (ib == 0 && tk >= 0 && tk < p.slots) tk_nr = __ldg(p.token_nr + tk);
       }
+      const int tok = tk_nr == 1 ? tk : -1;
       if (!aborted) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&ctl->sempty[uq]);
       }
       if (named_bar_or(1, 256, aborted)) break;
 
-      if (row < ti.rows) {
+      if (row < ti.rows && tok >= 0) {
+        // The token's only local route: its output columns nt * 256 .. + 255, as the combine would
+        // write them for a one-route token (0 + x, then one bf16 rounding or none).
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+#pragma unroll
+          for (int g = 0; g < 8; ++g) {
+            float v[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(0.0f, acc[h * 64 + 8 * g + i] * w);
+            const size_t col = static_cast<size_t>(tok) * H + nt * 256 + h * 128 + hf * 64 + 8 * g;
+            if (p.out_f32) {
+              st_global_v8(static_cast<float*>(p.out) + col, v);
+            } else {
+              uint4 b;
+              b.x = pack_bf16x2(v[0], v[1]);
+              b.y = pack_bf16x2(v[2], v[3]);
+              b.z = pack_bf16x2(v[4], v[5]);
+              b.w = pack_bf16x2(v[6], v[7]);
+              *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + col) = b;
+            }
+          }
+        }
+      } else if (row < ti.rows) {
         const size_t d = static_cast<size_t>(ctl->map.dense_off[e] + slot);
 #pragma unroll
         for (int h = 0; h < 2; ++h) {

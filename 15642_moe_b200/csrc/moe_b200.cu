@@ -49,6 +49,8 @@ int cuda_check(cudaError_t e, const char* what) {
 
 bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
 
+constexpr int DIRECT_MIN_TOKENS = 1024;
+
 // Scratch of moe_forward_noalloc, for callers that cannot allocate device memory. One copy
 // per device that loads this library, held until the process exits. Host code may not use the
 // array's name as a device address: the address comes from cudaGetSymbolAddress, taken once
@@ -316,8 +318,14 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   int* tile_ready = reinterpret_cast<int*>(W + ws.tile_ready);
   Gemm1Args g1{a_tiled, a_scale, static_cast<const uint8_t*>(w13_packed), w13_scale, counts, T,
                ws.tiles_max, E_local, c_hi, c_lo, c_scale, tile_ready};
+  // From DIRECT_MIN_TOKENS tokens on, GEMM2 writes the row of a token with one local route itself and
+  // the combine skips it (fewer fp32 route rows written and read back); below, where that saved
+  // little and GEMM2's extra loads cost a little, every route goes through `partial`. The results
+  // are the same either way.
+  const int direct = T >= DIRECT_MIN_TOKENS ? 1 : 0;
   Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, counts, T,
-               ws.tiles_max, E_local, route_w, partial, dense_base, tile_ready, tile_ready + ws.tiles_max};
+               ws.tiles_max, E_local, route_w, partial, dense_base, tile_ready, tile_ready + ws.tiles_max,
+               out_bf16, out_f32 ? 1 : 0, route_token, token_nr, direct};
 
   auto mark = [&](int i) {
     if (events != nullptr) cudaEventRecord(static_cast<cudaEvent_t>(events[i]), st);
@@ -353,10 +361,10 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   mark(4);
   if (out_f32)
     combine_kernel<float><<<T, COMBINE_THREADS, 0, st>>>(partial, token_nr, token_route, dense_base, T,
-                                                         E_local, static_cast<float*>(out_bf16));
+                                                         E_local, static_cast<float*>(out_bf16), direct);
   else
     combine_kernel<__nv_bfloat16><<<T, COMBINE_THREADS, 0, st>>>(partial, token_nr, token_route, dense_base,
-                                                                 T, E_local, static_cast<__nv_bfloat16*>(out_bf16));
+                                                                 T, E_local, static_cast<__nv_bfloat16*>(out_bf16), direct);
   mark(5);
   return cuda_check(cudaGetLastError(), "moe_forward launch");
 }
@@ -425,7 +433,7 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
                ws.tiles_max, L.e_rank, c_hi, c_lo, c_scale, tile_ready};
   Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, counts, L.r_cap,
                ws.tiles_max, L.e_rank, ep_at<float>(me, L.route_w), partial, dense_base, tile_ready,
-               tile_ready + ws.tiles_max};
+               tile_ready + ws.tiles_max, nullptr, 0, nullptr, nullptr, 0};
   // Source side: local slot claims over all 256 experts (route_kernel with E_local = 256).
   int* local_counts = reinterpret_cast<int*>(W + sw.local_counts);
   int* reserve_base = reinterpret_cast<int*>(W + sw.base);

@@ -328,6 +328,12 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float (&v)[32]) {
   for (int i = 0; i < 32; ++i) v[i] = __uint_as_float(r[i]);
 }
 
+// Two floats rounded to bf16 (nearest even), packed low word first.
+__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
+  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
 // acc[i] += v[i] * f for 32 values, as 16 packed fp32x2 FMAs (each lane IEEE fmaf).
 __device__ __forceinline__ void fma32_scaled(float* acc, const float (&v)[32], float f) {
   uint64_t ff;

@@ -275,11 +275,6 @@ __global__ void __launch_bounds__(256) gather_kernel(const uint8_t* __restrict__
 
 constexpr int COMBINE_THREADS = H / 16;  // 448 threads x 16 columns per row
 
-__device__ __forceinline__ uint32_t pack_bf16x2(float a, float b) {
-  __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
-  return *reinterpret_cast<uint32_t*>(&v);
-}
-
 // Row layout of the combine kernels: thread `tid` of a 448-thread CTA owns the four float4
 // column groups q = tid + 448 j (j = 0..3) of a 7168-wide row, i.e. columns 4q..4q+3; acc[4j + c]
 // is column 4q_j + c. A warp's access then covers 512 contiguous bytes per instruction.
@@ -347,9 +342,12 @@ __global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(const float* _
                                                                   const int* __restrict__ token_nr,
                                                                   const int* __restrict__ token_route,
                                                                   const int* __restrict__ dense_base,
-                                                                  int T, int E_local, OutT* __restrict__ out) {
+                                                                  int T, int E_local, OutT* __restrict__ out,
+                                                                  int skip_single) {
   const int t = blockIdx.x;
   if (t >= T) return;
+  // With skip_single, the GEMM2 kernel wrote the row of a token with exactly one local route.
+  if (skip_single && token_nr[t] == 1) return;
   const int tid = threadIdx.x;
   float acc[16];
 #pragma unroll

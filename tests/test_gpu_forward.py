@@ -163,6 +163,8 @@ def test_stages(pkg, oracle):
     nblk = (routes + 127) // 128
     partial = (region(ws, lay, "partial", torch.float32, nblk * 128 * 7168).reshape(nblk, 224, 128, 32)
                .transpose(0, 2, 1, 3).reshape(nblk * 128, 7168))
+    out_f = out.float().cpu().numpy()
+    assert (token_nr == 1).any() and (token_nr > 1).any()
     t0 = 0
     worst_c, worst_o = 0.0, 0.0
     for e in range(E):
@@ -180,10 +182,13 @@ def test_stages(pkg, oracle):
         worst_c = max(worst_c, float(err.max()))
         W2 = oracle.dequant_block(npi["gemm2_weights"][e], npi["gemm2_weights_scale"][e])
         Oe = (C @ W2.T) * route_w[e, :exp_counts[e]][:, None]
-        rel = np.abs(partial[drows] - Oe).max(axis=1) / (np.abs(Oe).max(axis=1) + 1e-30)
+        # a token's only local route goes straight to its output row (bf16); the others to `partial`
+        multi = token_nr[toks] > 1
+        got = np.where(multi[:, None], partial[drows], out_f[toks])
+        rel = np.abs(got - Oe).max(axis=1) / (np.abs(Oe).max(axis=1) + 1e-30)
         worst_o = max(worst_o, float(rel.max()))
         t0 += nt
-    print("worst C block-relative err", worst_c, "worst partial row-relative err", worst_o)
+    print("worst C block-relative err", worst_c, "worst route-row relative err", worst_o)
     assert worst_c < 2.0 ** -7
     assert worst_o < 1e-2
 
