@@ -336,24 +336,39 @@ __global__ void __launch_bounds__(G2_THREADS, 1) gemm2_weighted_kernel(const __g
 
       if (row < ti.rows && tok >= 0) {
         // The token's only local route: its output columns nt * 256 .. + 255, as the combine would
-        // write them for a one-route token (0 + x, then one bf16 rounding or none).
+        // write them for a one-route token (0 + x, then one bf16 rounding or none). The output is
+        // 16-byte aligned by contract; 256-bit stores only when it is also 32-byte aligned.
+        const bool out32 = (reinterpret_cast<uintptr_t>(p.out) & 31u) == 0;
 #pragma unroll
         for (int h = 0; h < 2; ++h) {
 #pragma unroll
-          for (int g = 0; g < 8; ++g) {
-            float v[8];
+          for (int g = 0; g < 8; g += 2) {
+            // 16 columns: 64 bytes of fp32 or 32 bytes of bf16 per store pair / store.
+            float v[16];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(0.0f, acc[h * 64 + 8 * g + i] * w);
+            for (int i = 0; i < 16; ++i) v[i] = __fadd_rn(0.0f, acc[h * 64 + 8 * g + i] * w);
             const size_t col = static_cast<size_t>(tok) * H + nt * 256 + h * 128 + hf * 64 + 8 * g;
             if (p.out_f32) {
-              st_global_v8(static_cast<float*>(p.out) + col, v);
+              float* o = static_cast<float*>(p.out) + col;
+              if (out32) {
+                st_global_v8(o, v);
+                st_global_v8(o + 8, v + 8);
+              } else {
+#pragma unroll
+                for (int i = 0; i < 4; ++i)
+                  reinterpret_cast<float4*>(o)[i] = make_float4(v[4 * i], v[4 * i + 1], v[4 * i + 2], v[4 * i + 3]);
+              }
             } else {
-              uint4 b;
-              b.x = pack_bf16x2(v[0], v[1]);
-              b.y = pack_bf16x2(v[2], v[3]);
-              b.z = pack_bf16x2(v[4], v[5]);
-              b.w = pack_bf16x2(v[6], v[7]);
-              *reinterpret_cast<uint4*>(static_cast<__nv_bfloat16*>(p.out) + col) = b;
+              uint32_t q[8];
+#pragma unroll
+              for (int i = 0; i < 8; ++i) q[i] = pack_bf16x2(v[2 * i], v[2 * i + 1]);
+              __nv_bfloat16* o = static_cast<__nv_bfloat16*>(p.out) + col;
+              if (out32) {
+                st_global_v8_u32(o, q);
+              } else {
+                reinterpret_cast<uint4*>(o)[0] = make_uint4(q[0], q[1], q[2], q[3]);
+                reinterpret_cast<uint4*>(o)[1] = make_uint4(q[4], q[5], q[6], q[7]);
+              }
             }
           }
         }

@@ -295,6 +295,10 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   const Workspace ws = make_workspace(T, E_local);
   if (workspace_bytes < ws.total)
     return fail(MOE_ERR_WORKSPACE, "workspace too small: need " + std::to_string(ws.total) + " bytes");
+  // Kernels store 32-byte vectors into workspace regions (at 1024-byte offsets): the base must be
+  // at least that aligned; 256 bytes is what cudaMalloc and the PyTorch allocator give.
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(MOE_ERR_INVALID, "moe_forward: workspace must be 256-byte aligned");
   DeviceInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
 
@@ -409,6 +413,8 @@ int ep_forward_impl(EpCtx* c, const void* hidden, const float* hidden_scale, con
   const EpSourceWs sw = make_ep_source_ws(ws.total, L.t_max);
   if (workspace_bytes < sw.total)
     return fail(MOE_ERR_WORKSPACE, "workspace too small: need " + std::to_string(sw.total) + " bytes");
+  if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
+    return fail(MOE_ERR_INVALID, "moe_ep_forward: workspace must be 256-byte aligned");
   int dev = -1;
   if (int rc = cuda_check(cudaGetDevice(&dev), "cudaGetDevice")) return rc;
   if (dev != c->device) return fail(MOE_ERR_INVALID, "moe_ep_forward: current device differs from the context's");

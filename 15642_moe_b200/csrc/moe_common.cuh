@@ -486,6 +486,12 @@ __host__ __device__ __forceinline__ size_t partial_offset(size_t d, int col) {
 }
 
 // 8 consecutive fp32 values to global memory in one 256-bit store (32-byte aligned address).
+// One 256-bit store of 8 words to a 32-byte aligned global address.
+__device__ __forceinline__ void st_global_v8_u32(void* p, const uint32_t* v) {
+  asm volatile("st.global.v8.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
 __device__ __forceinline__ void st_global_v8(float* p, const float* v) {
   asm volatile("st.global.v8.f32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8};" ::"l"(p), "f"(v[0]), "f"(v[1]), "f"(v[2]),
                "f"(v[3]), "f"(v[4]), "f"(v[5]), "f"(v[6]), "f"(v[7])

@@ -92,7 +92,8 @@ size_t moe_forward_workspace_bytes(int T, int E_local);
  *   out_bf16      bf16 [T, 7168]          (written completely; tokens without a local
  *                                          expert get zeros)
  *   T             0 <= T <= 65536
- * All device pointers 16-byte aligned. Asynchronous; no host synchronisation. */
+ * All device pointers 16-byte aligned, the workspace 256-byte aligned (as cudaMalloc returns).
+ * Asynchronous; no host synchronisation. */
 int moe_forward(const void* hidden, const float* hidden_scale, const void* w13_packed,
                 const float* w13_scale, const void* w2_packed, const float* w2_scale,
                 const float* logits, const float* bias, float routed_scaling_factor,
@@ -261,7 +262,8 @@ int moe_ep_info(void* ctx, int* out4);
  *   w13_packed / w2_packed: this rank's e_rank experts in placement order (moe_pack_w13 /
  *                 moe_pack_w2),
  *   w13_scale fp32 [e_rank, 32, 56], w2_scale fp32 [e_rank, 56, 16],
- *   out_bf16 bf16 [T, 7168]; workspace of moe_ep_workspace_bytes(world, t_rank_max, e_rank).
+ *   out_bf16 bf16 [T, 7168]; workspace of moe_ep_workspace_bytes(world, t_rank_max, e_rank),
+ *   256-byte aligned.
  * Asynchronous on `stream`; the call itself never waits for other ranks. No per-call host state:
  * the barriers' epoch is kept and advanced in device memory, so the call can be captured into a
  * CUDA graph (after one eager call for the per-device set-up) and the graph replayed, one epoch

@@ -84,3 +84,13 @@ def test_python_api_rejects_cpu_tensors(pkg):
         pkg.pack_w13(torch.zeros((1, 4096, 7000), dtype=torch.float8_e4m3fn))
     with pytest.raises(RuntimeError, match="FP8"):
         pkg.pack_w2(torch.zeros((1, 7168, 2048), dtype=torch.float32))
+
+
+def test_workspace_alignment_is_checked(pkg):
+    """The workspace must be 256-byte aligned (kernels store 32-byte vectors into it); a pointer
+    that is only 16-byte aligned is refused on the host before anything is launched."""
+    native = __import__("importlib").import_module("15642_moe_b200._native")
+    lib = native.cuda_lib()
+    p = 0x10000010   # host-side fake address: 16-byte aligned, not 256; nothing is dereferenced
+    rc = lib.moe_forward(p, p, p, p, p, p, p, p, 2.5, 0, 16, 32, p, p, 1 << 40, None)
+    assert rc == 1 and b"256-byte" in lib.moe_last_error()

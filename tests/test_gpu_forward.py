@@ -230,3 +230,27 @@ def test_forward_tile_size_boundaries(pkg, oracle):
     r = oracle.check_tolerance(ref, out_bits(out), ATOL, RTOL)
     print(r)
     assert r["bad"] == 0, r
+
+
+@pytest.mark.parametrize("fp32_out", [False, True])
+def test_output_16_byte_aligned_only(pkg, fp32_out):
+    """The output need only be 16-byte aligned. At T >= 1024 the GEMM2 kernel writes the rows of
+    one-route tokens itself; an output 16 bytes past a 32-byte boundary must give the same bits."""
+    T = 1024
+    inp = pkg.make_inputs(pkg.MoEConfig(T=T, seed=2), "cuda")
+    f32 = {k: inp[k].to(torch.float32).contiguous() for k in
+           ("hidden_states_scale", "gemm1_weights_scale", "gemm2_weights_scale", "routing_logits")}
+    args = (inp["hidden_states"].contiguous(), f32["hidden_states_scale"], pkg.pack_w13(inp["gemm1_weights"]),
+            f32["gemm1_weights_scale"], pkg.pack_w2(inp["gemm2_weights"]), f32["gemm2_weights_scale"],
+            f32["routing_logits"], inp["routing_bias"].to(torch.float32).reshape(-1).contiguous(),
+            float(inp["routed_scaling_factor"]), int(inp["local_expert_offset"]))
+    dtype = torch.float32 if fp32_out else torch.bfloat16
+    step = 16 // (4 if fp32_out else 2)
+    ref = pkg.moe_forward(*args, fp32_out=fp32_out)
+    big = torch.full((T * 7168 + step,), float("nan"), dtype=dtype, device="cuda")
+    out = big[step:].view(T, 7168)
+    assert out.data_ptr() % 32 == 16
+    pkg.moe_forward(*args, out=out, fp32_out=fp32_out)
+    torch.cuda.synchronize()
+    iview = torch.int32 if fp32_out else torch.int16
+    assert torch.equal(out.view(iview), ref.view(iview))
