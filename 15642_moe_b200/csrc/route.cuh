@@ -33,6 +33,28 @@ __device__ __forceinline__ uint32_t order_key(float v) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
+// Compare-exchange: entry a ends up the better of the two (larger key; on equal keys the lower
+// expert position), with its position and unbiased score alongside.
+__device__ __forceinline__ void cx_best(uint32_t& ka, int& pa, float& sa, uint32_t& kb, int& pb, float& sbv) {
+  const bool swap = kb > ka || (kb == ka && pb < pa);
+  const uint32_t k0 = swap ? kb : ka, k1 = swap ? ka : kb;
+  const int p0 = swap ? pb : pa, p1 = swap ? pa : pb;
+  const float s0 = swap ? sbv : sa, s1 = swap ? sa : sbv;
+  ka = k0; kb = k1; pa = p0; pb = p1; sa = s0; sbv = s1;
+}
+
+// Batcher's odd-even merge sort of eight entries (19 compare-exchanges), best first.
+__device__ __forceinline__ void sort8_best_first(uint32_t (&k)[8], int (&p)[8], float (&v)[8]) {
+#define MOE_CX(a, b) cx_best(k[a], p[a], v[a], k[b], p[b], v[b])
+  MOE_CX(0, 1); MOE_CX(2, 3); MOE_CX(4, 5); MOE_CX(6, 7);
+  MOE_CX(0, 2); MOE_CX(1, 3); MOE_CX(4, 6); MOE_CX(5, 7);
+  MOE_CX(1, 2); MOE_CX(5, 6);
+  MOE_CX(0, 4); MOE_CX(1, 5); MOE_CX(2, 6); MOE_CX(3, 7);
+  MOE_CX(2, 4); MOE_CX(3, 5);
+  MOE_CX(1, 2); MOE_CX(3, 4); MOE_CX(5, 6);
+#undef MOE_CX
+}
+
 // One warp per token; lane l owns experts 8l..8l+7, so a group of 32 experts is four lanes.
 // Outputs: topk_idx / topk_w [T, 8] in selection order. For the local picks (global expert g
 // with 0 <= le = g - local_offset < E_local), when `counts` is given: counts[le] (atomic),
@@ -111,31 +133,33 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
   // among the lanes holding it (ties to the lower index). Key 0 marks excluded or taken entries
   // (below every real score's key; biased scores are never -0.0, so equal keys mean equal
   // scores).
+  // Each lane first sorts its eight entries, best first (larger key, then lower expert index), so a
+  // round only reads the lane's head and the winning lane shifts its list by one.
   uint32_t key[8];
+  int pos[8];
+  float sv[8];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) key[i] = group_kept ? order_key(sb[i]) : 0u;
+  for (int i = 0; i < 8; ++i) {
+    key[i] = group_kept ? order_key(sb[i]) : 0u;
+    pos[i] = i;
+    sv[i] = s[i];
+  }
+  sort8_best_first(key, pos, sv);
   int sel_idx[TOP_K];
   float sel_s[TOP_K];
 #pragma unroll
   for (int k = 0; k < TOP_K; ++k) {
-    uint32_t lk = 0;
-    int li = 0;
-    float ls = 0.0f;
-#pragma unroll
-    for (int i = 0; i < 8; ++i) {
-      if (key[i] > lk) {  // strict: the lower i keeps a tie
-        lk = key[i];
-        li = i;
-        ls = s[i];
-      }
-    }
-    const uint32_t mk = __reduce_max_sync(0xffffffffu, lk);
-    const uint32_t wi = __reduce_min_sync(0xffffffffu, lk == mk ? static_cast<uint32_t>(lane * 8 + li) : 0xFFFFFFFFu);
-    const float ws = __shfl_sync(0xffffffffu, ls, static_cast<int>(wi >> 3));
+    const uint32_t mk = __reduce_max_sync(0xffffffffu, key[0]);
+    const uint32_t wi = __reduce_min_sync(0xffffffffu, key[0] == mk ? static_cast<uint32_t>(lane * 8 + pos[0]) : 0xFFFFFFFFu);
+    const float ws = __shfl_sync(0xffffffffu, sv[0], static_cast<int>(wi >> 3));
     if (static_cast<int>(wi >> 3) == lane) {
 #pragma unroll
-      for (int i = 0; i < 8; ++i)
-        if (i == static_cast<int>(wi & 7u)) key[i] = 0u;
+      for (int i = 0; i < 7; ++i) {
+        key[i] = key[i + 1];
+        pos[i] = pos[i + 1];
+        sv[i] = sv[i + 1];
+      }
+      key[7] = 0u;
     }
     sel_idx[k] = static_cast<int>(wi);
     sel_s[k] = ws;
