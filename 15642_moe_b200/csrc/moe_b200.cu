@@ -322,10 +322,11 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   int* tile_ready = reinterpret_cast<int*>(W + ws.tile_ready);
   Gemm1Args g1{a_tiled, a_scale, static_cast<const uint8_t*>(w13_packed), w13_scale, counts, T,
                ws.tiles_max, E_local, c_hi, c_lo, c_scale, tile_ready};
-  // From DIRECT_MIN_TOKENS tokens on, GEMM2 writes the row of a token with one local route itself and
-  // the combine skips it (fewer fp32 route rows written and read back); below, where that saved
-  // little and GEMM2's extra loads cost a little, every route goes through `partial`. The results
-  // are the same either way.
+  // From DIRECT_MIN_TOKENS tokens on, GEMM2 writes the row of a token with one local route itself,
+  // the router writes the zero row of a token with none, and the combine skips both (fewer fp32
+  // route rows written and read back, fewer combine blocks); below, where that saved little and
+  // GEMM2's extra loads cost a little, every token goes through the combine. The results are the
+  // same either way.
   const int direct = T >= DIRECT_MIN_TOKENS ? 1 : 0;
   Gemm2Args g2{c_hi, c_lo, c_scale, static_cast<const uint8_t*>(w2_packed), w2_scale, counts, T,
                ws.tiles_max, E_local, route_w, partial, dense_base, tile_ready, tile_ready + ws.tiles_max,
@@ -342,7 +343,8 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   else
     route_kernel<<<(T + 7) / 8, 256, 0, st>>>(logits, bias, T, routed_scaling_factor, local_expert_offset,
                                               E_local, topk_idx, topk_w, counts, token_nr, token_route,
-                                              route_token, route_w);
+                                              route_token, route_w, direct ? out_bf16 : nullptr,
+                                              out_f32 ? H * 4 : H * 2);
   mark(1);
   const size_t route_max = static_cast<size_t>(T) * (E_local < TOP_K ? E_local : TOP_K);
   // gather and GEMM1 are launched programmatically: each may be scheduled while its predecessor

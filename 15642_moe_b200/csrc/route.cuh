@@ -60,6 +60,8 @@ __device__ __forceinline__ void sort8_best_first(uint32_t (&k)[8], int (&p)[8], 
 // with 0 <= le = g - local_offset < E_local), when `counts` is given: counts[le] (atomic),
 // route_token[le * T + slot] = t, route_w[le * T + slot] = weight, and the token's own list
 // token_route[t * 8 + k] = (le << 16) | slot in ascending le, token_nr[t] = its length.
+// When `zero_out` is given (rows of `zero_row_bytes`, 16-byte aligned), the output row of a token
+// without a local route is written here as +0, and the combine skips that token.
 __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ logits,
                                                     const float* __restrict__ bias, int T,
                                                     float rsf, int local_offset, int E_local,
@@ -69,7 +71,9 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
                                                     int* __restrict__ token_nr,
                                                     int* __restrict__ token_route,
                                                     int* __restrict__ route_token,
-                                                    float* __restrict__ route_w) {
+                                                    float* __restrict__ route_w,
+                                                    void* __restrict__ zero_out = nullptr,
+                                                    int zero_row_bytes = 0) {
   // The gather kernel may be scheduled once every block of this grid runs; it waits for this
   // grid's completion in hardware before reading anything written here.
   if (threadIdx.x == 0) allow_dependent_launch();
@@ -220,6 +224,19 @@ __global__ void __launch_bounds__(256) route_kernel(const float* __restrict__ lo
     }
   }
   if (lane == 0 && token_nr != nullptr) token_nr[t] = nlocal;
+  // A token without a local route: its output row is +0 (the combine's sum from +0 over no
+  // routes). The router is bound by its load latency, so these stores cost it little, and the
+  // combine no longer spends a block on each such token.
+  if (zero_out != nullptr && nlocal == 0) {
+    uint8_t* row = static_cast<uint8_t*>(zero_out) + static_cast<size_t>(t) * zero_row_bytes;
+    if ((reinterpret_cast<uintptr_t>(zero_out) & 31u) == 0) {
+      const uint32_t z[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      for (int b = lane * 32; b < zero_row_bytes; b += 32 * 32) st_global_v8_u32(row + b, z);
+    } else {
+      for (int b = lane * 16; b < zero_row_bytes; b += 32 * 16)
+        *reinterpret_cast<uint4*>(row + b) = make_uint4(0, 0, 0, 0);
+    }
+  }
 }
 
 // Routing of the shared expert: every token is slot t of the single local expert, weight 1.
@@ -367,11 +384,12 @@ __global__ void __launch_bounds__(COMBINE_THREADS) combine_kernel(const float* _
                                                                   const int* __restrict__ token_route,
                                                                   const int* __restrict__ dense_base,
                                                                   int T, int E_local, OutT* __restrict__ out,
-                                                                  int skip_single) {
+                                                                  int skip_written) {
   const int t = blockIdx.x;
   if (t >= T) return;
-  // With skip_single, the GEMM2 kernel wrote the row of a token with exactly one local route.
-  if (skip_single && token_nr[t] == 1) return;
+  // With skip_written, the row of a token with one local route was written by the GEMM2 kernel
+  // and that of a token with none by the router.
+  if (skip_written && token_nr[t] <= 1) return;
   const int tid = threadIdx.x;
   float acc[16];
 #pragma unroll

@@ -235,7 +235,8 @@ def test_forward_tile_size_boundaries(pkg, oracle):
 @pytest.mark.parametrize("fp32_out", [False, True])
 def test_output_16_byte_aligned_only(pkg, fp32_out):
     """The output need only be 16-byte aligned. At T >= 1024 the GEMM2 kernel writes the rows of
-    one-route tokens itself; an output 16 bytes past a 32-byte boundary must give the same bits."""
+    one-route tokens itself and the router the zero rows of tokens without a local route; an
+    output 16 bytes past a 32-byte boundary must give the same bits, with no row left unwritten."""
     T = 1024
     inp = pkg.make_inputs(pkg.MoEConfig(T=T, seed=2), "cuda")
     f32 = {k: inp[k].to(torch.float32).contiguous() for k in
@@ -254,3 +255,6 @@ def test_output_16_byte_aligned_only(pkg, fp32_out):
     torch.cuda.synchronize()
     iview = torch.int32 if fp32_out else torch.int16
     assert torch.equal(out.view(iview), ref.view(iview))
+    assert not torch.isnan(out.float()).any()               # every row written over the NaN fill
+    zero_rows = (out.view(iview) == 0).all(dim=1).sum().item()
+    assert zero_rows > 0                                     # tokens without a local route: +0 rows
