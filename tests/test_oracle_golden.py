@@ -107,3 +107,18 @@ def test_oracle_matches_reference_on_its_own_generator(name, oracle):
     ulp = np.abs(oracle.bf16_bits_to_f32(g["out_bf16"])) * 2.0 ** -7 + 2.0 ** -20
     assert (diff <= ulp).all(), float(diff.max())
     assert (out == g["out_bf16"]).mean() > 0.99
+
+
+@pytest.mark.parametrize("name", FULL + REF_FULL)
+def test_reference_rows_without_local_routes_are_plus_zero(name):
+    """The reference's output starts as a zero tensor and only local routes add to it
+    (reference/moe_ref.py:110-136), so a token without a local route gets the bf16 bits of +0
+    and every other token a row that is not all zeros. The CUDA path writes such rows directly
+    (without summing anything) from 1024 tokens on; this pins that they must be exactly +0."""
+    g, cfg = load(name)
+    off = cfg.get("local_expert_offset", 0)
+    e_local = cfg.get("E_local", 32)                  # the reference generator's 32 local experts
+    idx = g["topk_sorted"].astype(np.int64)
+    nlocal = ((idx >= off) & (idx < off + e_local)).sum(axis=1)
+    rows_zero = (g["out_bf16"] == 0).all(axis=1)
+    np.testing.assert_array_equal(rows_zero, nlocal == 0)
