@@ -90,7 +90,9 @@ size_t moe_forward_workspace_bytes(int T, int E_local);
  *   logits        fp32 [T, 256],          bias      fp32 [256]
  *   routed_scaling_factor, local_expert_offset: as reference/moe_ref.py:14-15
  *   out_bf16      bf16 [T, 7168]          (written completely; tokens without a local
- *                                          expert get zeros)
+ *                                          expert get zeros; from 1024 tokens on, rows are
+ *                                          written while inputs are still being read, so it
+ *                                          must not overlap any input or the workspace)
  *   T             0 <= T <= 65536
  * All device pointers 16-byte aligned, the workspace 256-byte aligned (as cudaMalloc returns).
  * Asynchronous; no host synchronisation. */
