@@ -94,3 +94,48 @@ def test_workspace_alignment_is_checked(pkg):
     p = 0x10000010   # host-side fake address: 16-byte aligned, not 256; nothing is dereferenced
     rc = lib.moe_forward(p, p, p, p, p, p, p, p, 2.5, 0, 16, 32, p, p, 1 << 40, None)
     assert rc == 1 and b"256-byte" in lib.moe_last_error()
+
+
+@pytest.mark.parametrize("T,E", [(0, 32), (1, 1), (1, 32), (7, 3), (64, 32), (1000, 8), (1024, 32),
+                                 (4096, 32), (16384, 256), (65536, 32), (65536, 256)])
+def test_workspace_layout_covers_every_region(pkg, T, E):
+    """Each scratch region holds the largest index its kernels address, for any routing: the
+    per-expert 128-row tiles (each active expert pads its rows up to a multiple of 128), the dense
+    route rows of `partial` in blocks of 128 rows x 224 groups of 32 floats, and the slot lists.
+    Regions start on 1024-byte boundaries, so 256-bit stores at 32-byte offsets inside them stay
+    aligned on a 256-byte aligned workspace."""
+    import random
+    native = __import__("importlib").import_module("15642_moe_b200._native")
+    lay = native.workspace_layout(T, E)
+    order = ["counts", "dense_base", "topk_idx", "topk_w", "token_nr", "token_route", "route_token",
+             "route_w", "a_tiled", "a_scale", "c_hi", "c_lo", "c_scale", "partial", "tile_ready", "total"]
+    offs = [lay[k] for k in order]
+    assert offs == sorted(offs) and all(v % 1024 == 0 for v in offs)
+    size = {k: lay[order[i + 1]] - lay[k] for i, k in enumerate(order[:-1])}
+    kmax = min(E, 8)
+    routes = T * kmax
+    active = min(routes, E)
+    tiles = (routes + active * 127 + 127) // 128
+    need = {
+        "counts": 4 * E, "dense_base": 4 * (E + 1), "topk_idx": 4 * 8 * T, "topk_w": 4 * 8 * T,
+        "token_nr": 4 * T, "token_route": 4 * 8 * T, "route_token": 4 * E * T, "route_w": 4 * E * T,
+        "a_tiled": tiles * 56 * 128 * 128, "a_scale": 4 * tiles * 56 * 128,
+        "c_hi": tiles * 16 * 128 * 128, "c_lo": tiles * 16 * 128 * 128, "c_scale": 4 * tiles * 16 * 128,
+        "partial": 4 * ((routes + 127) // 128) * 128 * 7168, "tile_ready": 4 * (tiles + 1),
+    }
+    for k, n in need.items():
+        assert size[k] >= n, (k, size[k], n)
+    if routes:
+        # The last float a route row can address (partial_offset of dense row routes - 1, column 7167).
+        d, col = routes - 1, 7167
+        last = ((d // 128 * 224 + (col >> 5)) * 128 + d % 128) * 32 + (col & 31)
+        assert 4 * (last + 1) <= size["partial"]
+    # Any split of the routes over the experts fits in the tiles the layout provides.
+    rng = random.Random(T * 1000 + E)
+    for _ in range(20):
+        counts = [0] * E
+        for _ in range(min(routes, 4096)):
+            counts[rng.randrange(E)] += 1
+        scale = routes / max(1, sum(counts))
+        counts = [min(T, int(c * scale)) for c in counts]
+        assert sum((c + 127) // 128 for c in counts) <= tiles
