@@ -299,6 +299,30 @@ int forward_impl(const void* hidden, const float* hidden_scale, const void* w13_
   // at least that aligned; 256 bytes is what cudaMalloc and the PyTorch allocator give.
   if ((reinterpret_cast<uintptr_t>(workspace) & 255u) != 0)
     return fail(MOE_ERR_INVALID, "moe_forward: workspace must be 256-byte aligned");
+  // Output rows are written while inputs are still being read (the router's zero rows before the
+  // gather reads the hidden rows), so the output may overlap no input and not the workspace.
+  {
+    const size_t e = static_cast<size_t>(E_local), t = static_cast<size_t>(T);
+    const struct {
+      const void* p;
+      size_t n;
+    } in[] = {{hidden, t * H},
+              {hidden_scale, sizeof(float) * HB * t},
+              {w13_packed, e * 2 * I * H},
+              {w13_scale, sizeof(float) * e * 2 * IB * HB},
+              {w2_packed, e * H * I},
+              {w2_scale, sizeof(float) * e * HB * IB},
+              {logits, shared ? 0 : sizeof(float) * t * E_GLOBAL},
+              {bias, shared ? 0 : sizeof(float) * E_GLOBAL},
+              {workspace, ws.total}};
+    const uintptr_t o0 = reinterpret_cast<uintptr_t>(out_bf16);
+    const uintptr_t o1 = o0 + t * H * (out_f32 ? sizeof(float) : sizeof(uint16_t));
+    for (const auto& r : in) {
+      const uintptr_t a0 = reinterpret_cast<uintptr_t>(r.p);
+      if (r.n != 0 && a0 < o1 && o0 < a0 + r.n)
+        return fail(MOE_ERR_INVALID, "moe_forward: the output overlaps an input or the workspace");
+    }
+  }
   DeviceInfo* d = nullptr;
   if (int rc = device_info(&d)) return rc;
 

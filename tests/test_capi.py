@@ -139,3 +139,35 @@ def test_workspace_layout_covers_every_region(pkg, T, E):
         scale = routes / max(1, sum(counts))
         counts = [min(T, int(c * scale)) for c in counts]
         assert sum((c + 127) // 128 for c in counts) <= tiles
+
+
+def test_output_overlapping_an_input_is_refused(pkg):
+    """Output rows are written while inputs are still being read, so an output that overlaps an
+    input or the workspace is refused on the host, before anything is launched (fake addresses:
+    nothing is dereferenced)."""
+    native = __import__("importlib").import_module("15642_moe_b200._native")
+    lib = native.cuda_lib()
+    T, E = 16, 32
+    ws = lib.moe_forward_workspace_bytes(T, E)
+    base = 1 << 36
+    names = ["hidden", "hidden_scale", "w13", "w13_scale", "w2", "w2_scale", "logits", "bias", "ws"]
+    sizes = [T * 7168, 4 * 56 * T, E * 4096 * 7168, 4 * E * 32 * 56, E * 7168 * 2048, 4 * E * 56 * 16,
+             4 * T * 256, 4 * 256, ws]
+    addr, a = {}, base
+    for n, s in zip(names, sizes):
+        addr[n] = a
+        a += (s + 4095) // 4096 * 4096 + 4096
+    out_free = a
+
+    def call(out):
+        v = addr
+        return lib.moe_forward(v["hidden"], v["hidden_scale"], v["w13"], v["w13_scale"], v["w2"],
+                               v["w2_scale"], v["logits"], v["bias"], 2.5, 0, T, E, out, v["ws"], ws, None)
+
+    # Every case here is refused on the host: a call whose fake addresses passed every host check
+    # would launch kernels on them where a GPU is present, so no such call is made.
+    for n, s in zip(names, sizes):
+        for out in (addr[n], addr[n] + s - 16, addr[n] - T * 7168 * 2 + 16):
+            rc = call(out)
+            assert rc == 1 and b"overlaps" in lib.moe_last_error(), (n, out - addr[n])
+    assert out_free > addr["ws"] + ws                 # the layout above keeps the ranges apart
