@@ -92,7 +92,8 @@ size_t moe_forward_workspace_bytes(int T, int E_local);
  *   out_bf16      bf16 [T, 7168]          (written completely; tokens without a local
  *                                          expert get zeros; from 1024 tokens on, rows are
  *                                          written while inputs are still being read, so it
- *                                          must not overlap any input or the workspace)
+ *                                          must not overlap any input or the workspace:
+ *                                          refused with MOE_ERR_INVALID)
  *   T             0 <= T <= 65536
  * All device pointers 16-byte aligned, the workspace 256-byte aligned (as cudaMalloc returns).
  * Asynchronous; no host synchronisation. */
